@@ -1,0 +1,490 @@
+#!/usr/bin/env python
+"""Benchmark of the fused linear + CE + entropy engine (one JSON line on rank 0).
+
+Workload: B=32768, H=4096, V=128256, bf16, chunk 4096; hidden ~ N(0,1),
+weight ~ N(0, 0.02), targets uniform. One step = one forward over the whole batch through the
+public API (`gemm_fused_ce_entropy`; vocabulary-parallel `vocab_parallel_ce_entropy` for N > 1).
+The same line also reports the training step (`gemm_megakernel_fast` + loss.backward(), configs[2])
+under "fwd_bwd".
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (vocabulary sharded over N GPUs)
+
+Timing: CUDA events on the launching stream, barrier + synchronize on both sides, max over ranks.
+Inputs (1 GiB weight, 256 MiB hidden) are far larger than L2, so no flush is needed between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "fast-reduction_b200"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "fwd & fwd+bwd ms @B32768 H4096 V128256 bf16; % dense BF16 tensor peak"
+WORKLOAD = "configs[1] forward headline: B=32768 H=4096 V=128256 bf16 chunk 4096"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------------------------------------ utils
+def load_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        d["source"] = "measured"
+        return d
+    return dict(FALLBACK_PEAKS)
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    if world != n_gpus and rank == 0:
+        print(f"[bench] note: --gpus {n_gpus} but WORLD_SIZE={world}; using {world}", file=sys.stderr)
+    return world, rank, local
+
+
+def barrier(world: int):
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while a timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sms, maxes, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in csv.reader(io.StringIO(out)):
+            if len(row) < 9:
+                continue
+            try:
+                sm = float(row[1])
+                mx = float(row[2])
+            except ValueError:
+                continue
+            sms.append(sm)
+            maxes.append(mx)
+            try:
+                power.append(float(row[3]))
+            except ValueError:
+                pass
+            for n, v in zip(names, row[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = ([s for s, p in zip(sms, power) if p > 300] or sms) if len(power) == len(sms) else sms
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms), "power_w_max": max(power) if power else None}
+
+
+class KernelTimer:
+    """Launch observer for fast_reduction.ops: CUDA events around every libfrx launch."""
+
+    def __init__(self):
+        self.pending = []
+        self.count = 0
+
+    def before(self, name, dev):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(dev))
+        self.pending.append([name, ev, None])
+
+    def after(self, name, dev):
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(torch.cuda.current_stream(dev))
+        self.pending[-1][2] = ev
+        self.count += 1
+
+    def summary(self) -> dict:
+        torch.cuda.synchronize()
+        out = {}
+        for name, a, b in self.pending:
+            d = out.setdefault(name, {"launches": 0, "total_ms": 0.0})
+            d["launches"] += 1
+            d["total_ms"] += a.elapsed_time(b)
+        return out
+
+
+def time_steps(step, steps: int, warmup: int, world: int, timer: KernelTimer | None = None, sampler=None):
+    from fast_reduction import ops
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler is not None:
+        sampler.start()
+    prev = ops.set_launch_observer(timer) if timer is not None else None
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step()
+    end.record()
+    torch.cuda.synchronize()
+    if timer is not None:
+        ops.set_launch_observer(prev)
+    clocks = sampler.stop() if sampler is not None else None
+    barrier(world)
+    ms = start.elapsed_time(end) / steps
+    return max_over_ranks(ms, world), clocks
+
+
+# ------------------------------------------------------------------------------------------------ inputs
+def make_headline_inputs(B, H, V, vstart, vend, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    hidden = torch.randn(B, H, device="cuda", generator=g).to(torch.bfloat16)
+    weight = torch.empty(vend - vstart, H, device="cuda", dtype=torch.bfloat16)
+    # the full weight is drawn in row blocks so every rank sees the same slice values for any N
+    blk = 8192
+    for r0 in range(0, V, blk):
+        r1 = min(r0 + blk, V)
+        gb = torch.Generator(device="cuda").manual_seed(seed * 1_000_003 + r0 + 1)
+        lo, hi = max(r0, vstart), min(r1, vend)
+        if lo >= hi:
+            continue
+        rows = (torch.randn(r1 - r0, H, device="cuda", generator=gb) * 0.02).to(torch.bfloat16)
+        weight[lo - vstart:hi - vstart] = rows[lo - r0:hi - r0]
+    target = torch.randint(0, V, (B,), device="cuda", generator=g)
+    return hidden, weight, target
+
+
+# ------------------------------------------------------------------------------------------------ cpu baseline
+def cpu_baseline(B, H, V, chunk, budget_s: float = 12.0) -> dict:
+    """Times the oracle port of the reference's chunked torch path (baseline.py:207-241) on the
+    host cores over a row sample of the headline workload, extrapolated linearly to B rows."""
+    from oracle import reference_math as rm
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    weight = (torch.randn(V, H, generator=g) * 0.02).to(torch.bfloat16)
+    rows = 64
+    h = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    t = torch.randint(0, V, (rows,), generator=g)
+    t0 = time.perf_counter()
+    rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
+    probe = time.perf_counter() - t0
+    rows = int(max(64, min(4096, rows * budget_s / max(probe, 1e-3)))) // 64 * 64
+    h = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    t = torch.randint(0, V, (rows,), generator=g)
+    t0 = time.perf_counter()
+    rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
+    el = time.perf_counter() - t0
+    ms_full = el * 1000.0 * B / rows
+    return {"value": round(ms_full, 1), "unit": "ms", "cores": threads, "kind": "port",
+            "sample": f"{rows} of {B} rows (full V={V}, H={H}) in {el:.1f} s on {threads} threads, "
+                      f"extrapolated linearly to B={B}; oracle/reference_math.chunked_linear_xent_entropy "
+                      f"(restates reference baseline.py:207-241), torch CPU bf16 matmul"}
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the reference's own algorithm for this path on the host cores (the oracle
+    port of baseline.chunked_linear_xent_entropy; the reference's Python cannot travel to the box)."""
+    if rank != 0:
+        return
+    from oracle import reference_math as rm
+
+    B, H, V, chunk = args.B, args.H, args.V, args.chunk
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    weight = (torch.randn(V, H, generator=g) * 0.02).to(torch.bfloat16)
+    # size one step (a row sample) for ~3 s of CPU work so warmup + steps finish in minutes
+    h = torch.randn(64, H, generator=g).to(torch.bfloat16)
+    t = torch.randint(0, V, (64,), generator=g)
+    t0 = time.perf_counter()
+    rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
+    probe = time.perf_counter() - t0
+    rows = int(max(64, min(2048, 64 * 3.0 / max(probe, 1e-3)))) // 64 * 64
+    h = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    t = torch.randint(0, V, (rows,), generator=g)
+    for _ in range(args.warmup):
+        rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
+        times.append(time.perf_counter() - t0)
+    per_step = statistics.median(times)
+    ms_full = per_step * 1000.0 * B / rows
+    flops = 2.0 * B * H * V
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(ms_full, 1), "unit": "ms", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_full, 1), "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "B": B, "H": H, "V": V, "chunk": chunk, "parallelism": "cpu",
+                   "l2": "inputs larger than L2"},
+        "tflops": round(flops / (ms_full / 1000.0) / 1e12, 3),
+        "cpu_baseline": {"value": round(ms_full, 1), "unit": "ms", "cores": threads, "kind": "port",
+                         "sample": f"each step: {rows} of {B} rows (full V, H), median of {args.steps} steps "
+                                   f"= {per_step:.2f} s, extrapolated linearly to B={B}"},
+        "e2e": {"value": round(ms_full, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------ our engine
+def run_ours(args, world, rank, local):
+    from fast_reduction import _native as nat
+    from fast_reduction import gemm_kernel as gk
+    from fast_reduction import vocab_parallel as vp
+
+    nat.load()
+    B, H, V, chunk = args.B, args.H, args.V, args.chunk
+    vstart, vend = vp.shard_bounds(V, world, rank)
+    Vr = vend - vstart
+    peaks = load_peaks()
+    hidden, weight, target = make_headline_inputs(B, H, V, vstart, vend, seed=0)
+    torch.cuda.synchronize()
+
+    if world == 1:
+        def fwd():
+            return gk.gemm_fused_ce_entropy(hidden, weight, target, chunk_size=chunk)
+    else:
+        def fwd():
+            return vp.vocab_parallel_ce_entropy(hidden, weight, target, vstart, V, chunk_size=chunk)
+
+    # ---- forward (headline value) with per-kernel event timing and clock sampling
+    timer = KernelTimer()
+    sampler = ClockSampler(local)
+    fwd_ms, clocks = time_steps(fwd, args.steps, args.warmup, world, timer, sampler)
+    ksum = timer.summary()
+    launches_fwd = timer.count
+    flops_fwd = 2.0 * B * H * V
+    gemm = ksum.get("fwd_partials", {"launches": 1, "total_ms": float("nan")})
+    gemm_avg_ms = gemm["total_ms"] / max(gemm["launches"], 1)
+    rows_per_launch = min(chunk, B)
+    gemm_flops = 2.0 * rows_per_launch * Vr * H
+    achieved_tflops = gemm_flops / (gemm_avg_ms / 1000.0) / 1e12
+    peak_tf = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+
+    # accuracy spot check on 512 rows against fp32 torch (TF32 off)
+    ce, ent, lp = fwd()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    acc = {}
+    if world == 1:
+        n = 512
+        z = hidden[:n].float() @ weight.float().T
+        lse = torch.logsumexp(z, -1)
+        ls = z - lse[:, None]
+        ce32 = lse - z[torch.arange(n, device=z.device), target[:n]]
+        ent32 = -(ls.exp() * ls).sum(-1)
+        acc = {"ce_mae": float((ce[:n] - ce32).abs().mean()), "ent_mae": float((ent[:n] - ent32).abs().mean()),
+               "rows_checked": n}
+        del z, ls
+
+    # ---- fwd+bwd (training step, configs[2])
+    fb = None
+    if not args.no_fwd_bwd:
+        h_leaf = hidden.detach().requires_grad_(True)
+        w_leaf = weight.detach().requires_grad_(True)
+
+        if world == 1:
+            def train_step():
+                h_leaf.grad = None
+                w_leaf.grad = None
+                loss, _, _ = gk.gemm_megakernel_fast(h_leaf, w_leaf, target, chunk_size=chunk)
+                loss.backward()
+        else:
+            def train_step():
+                h_leaf.grad = None
+                w_leaf.grad = None
+                loss, _, _ = vp.vocab_parallel_megakernel(h_leaf, w_leaf, target, vstart, V, chunk_size=chunk)
+                loss.backward()
+
+        timer_fb = KernelTimer()
+        fb_steps = max(1, min(args.steps, 10))
+        fb_ms, fb_clocks = time_steps(train_step, fb_steps, max(args.warmup, 1), world, timer_fb, ClockSampler(local))
+        kfb = timer_fb.summary()
+        flops_fb = 6.0 * B * H * V
+        fb = {"ms": round(fb_ms, 3), "tflops": round(flops_fb / (fb_ms / 1000.0) / 1e12, 1),
+              "frac_of_peak": round(flops_fb / (fb_ms / 1000.0) / 1e12 / peak_tf, 4), "steps": fb_steps,
+              "workload": "configs[2] gemm_megakernel_fast + loss.backward(), ce_weight 1, ent_weight -1",
+              "kernels_ms_per_step": {k: round(v["total_ms"] / fb_steps, 3) for k, v in kfb.items()},
+              "gpu_launches_per_step": timer_fb.count // fb_steps, "clocks": fb_clocks}
+        if world == 1:
+            n = 256
+            hs = hidden[:n].detach().float().requires_grad_(True)
+            z = hs @ weight.float().T
+            ls = torch.log_softmax(z, -1)
+            l = torch.nn.functional.nll_loss(ls, target[:n], reduction="sum") + (ls.exp() * ls).sum()
+            l.backward()
+            train_step()
+            fb["dh_mae_rows_checked"] = n
+            fb["dh_mae"] = float((h_leaf.grad[:n].float() - hs.grad).abs().mean())
+            fb["dh_rel_err"] = float((h_leaf.grad[:n].float() - hs.grad).norm() / hs.grad.norm())
+            del z, ls, hs
+        h_leaf.grad = None
+        w_leaf.grad = None
+        del h_leaf, w_leaf
+
+    # ---- end to end through the public API with host buffers (H2D inputs, D2H results inside)
+    e2e = None
+    if not args.no_e2e:
+        h_host = hidden.cpu().pin_memory()
+        w_host = weight.cpu().pin_memory()
+        t_host = target.cpu().pin_memory()
+        outs_host = [torch.empty(B, dtype=torch.float32).pin_memory() for _ in range(3)]
+
+        def e2e_step():
+            h_d = h_host.to("cuda", non_blocking=True)
+            w_d = w_host.to("cuda", non_blocking=True)
+            t_d = t_host.to("cuda", non_blocking=True)
+            if world == 1:
+                res = gk.gemm_fused_ce_entropy(h_d, w_d, t_d, chunk_size=chunk)
+            else:
+                res = vp.vocab_parallel_ce_entropy(h_d, w_d, t_d, vstart, V, chunk_size=chunk)
+            for o, r in zip(outs_host, res):
+                o.copy_(r, non_blocking=True)
+
+        e2e_ms, _ = time_steps(e2e_step, max(1, min(args.steps, 10)), max(args.warmup, 1), world)
+        h2d = h_host.numel() * 2 + w_host.numel() * 2 + t_host.numel() * 8
+        e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(3 * B * 4),
+               "path": "pinned host hidden/weight(shard)/target -> gemm_fused_ce_entropy -> pinned host ce/ent/logp"}
+        del h_host, w_host, t_host, outs_host
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(B, H, V, chunk)
+
+    traffic = None
+    tp = REPO / "profiles" / "traffic.json"
+    if tp.exists():
+        try:
+            tj = json.loads(tp.read_text())
+            ent_ = tj.get("fwd_partials")
+            if ent_ and ent_.get("rows_per_launch") and Vr == ent_.get("vocab_shard", Vr):
+                traffic = ent_["dram_bytes_per_launch"] * rows_per_launch / ent_["rows_per_launch"]
+        except Exception:
+            traffic = None
+
+    if rank != 0:
+        return
+    tflops = flops_fwd / (fwd_ms / 1000.0) / 1e12
+    line = {
+        "metric": METRIC,
+        "value": round(fwd_ms, 3),
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(fwd_ms, 3),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded: hidden N(0,1), weight N(0,0.02), uniform targets)",
+        "config": {"workload": WORKLOAD, "B": B, "H": H, "V": V, "chunk": chunk,
+                   "parallelism": f"vocab-sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (no flush needed)"},
+        "tflops": round(tflops, 1),
+        "frac_of_peak": round(tflops / peak_tf, 4),
+        "peak_bf16_tflops": peak_tf,
+        "peak_source": peaks.get("source"),
+        "roofline": {"bound": "tensor", "kernel": "gemm_tcgen05_kernel<CEPartialsEpilogue> (frx_fwd_partials)",
+                     "achieved": round(achieved_tflops, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                     "frac": round(achieved_tflops / peak_tf, 4), "traffic": traffic,
+                     "algorithmic_flop_per_launch": gemm_flops, "avg_launch_ms": round(gemm_avg_ms, 4),
+                     "launches_timed": gemm["launches"]},
+        "kernels_ms_per_step": {k: round(v["total_ms"] / args.steps, 4) for k, v in ksum.items()},
+        "gpu_launches": launches_fwd,
+        "clocks": clocks,
+        "accuracy": acc,
+        "fwd_bwd": fb,
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--B", type=int, default=32768)
+    ap.add_argument("--H", type=int, default=4096)
+    ap.add_argument("--V", type=int, default=128256)
+    ap.add_argument("--chunk", type=int, default=4096)
+    ap.add_argument("--no-fwd-bwd", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,81 @@
+// Library-wide host plumbing: error string, version, device attribute cache and TMA
+// descriptor encoding (cuTensorMapEncodeTiled is fetched through the runtime's driver
+// entry-point query, so the library does not link libcuda directly).
+#include <cstring>
+
+#include "frx_host.cuh"
+
+namespace frx {
+
+namespace {
+thread_local char g_last_error[512] = {0};
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+std::atomic<int> g_sm_count[64];
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+}
+
+int sm_count(int* out) {
+  int dev = 0;
+  FRX_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 64) {
+    int cached = g_sm_count[dev].load(std::memory_order_relaxed);
+    if (cached > 0) {
+      *out = cached;
+      return FRX_OK;
+    }
+  }
+  int n = 0;
+  FRX_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  if (dev < 64) g_sm_count[dev].store(n, std::memory_order_relaxed);
+  *out = n;
+  return FRX_OK;
+}
+
+int encode_bf16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                   int box_cols) {
+  EncodeTiledFn fn = get_encode_fn();
+  FRX_REQUIRE(fn != nullptr, FRX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+  FRX_REQUIRE(aligned16(base), FRX_ERR_INVALID_ARG, "bf16 operand base %p is not 16-byte aligned", base);
+  FRX_REQUIRE(ld % 8 == 0, FRX_ERR_INVALID_ARG, "bf16 operand leading dimension %lld is not a multiple of 8",
+              (long long)ld);
+  FRX_REQUIRE(rows >= 1 && cols >= 1 && ld >= cols, FRX_ERR_INVALID_ARG,
+              "bad operand extents rows=%lld cols=%lld ld=%lld", (long long)rows, (long long)cols, (long long)ld);
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld) * 2u};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FRX_REQUIRE(r == CUDA_SUCCESS, FRX_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+  return FRX_OK;
+}
+
+}  // namespace frx
+
+extern "C" int frx_abi_version(void) { return FRX_ABI_VERSION; }
+
+extern "C" const char* frx_last_error(void) { return frx::g_last_error; }

@@ -1,0 +1,138 @@
+// Backward contractions of the training path, both on the tcgen05 GEMM core:
+//
+//   d_hidden[B, H] = dlogits[B, V] @ weight[V, H]      A = dlogits (K-major), B = weight (MN-major)
+//   d_weight[V, H] = dlogits[B, V]^T @ hidden[B, H]    A = dlogits (MN-major), B = hidden (MN-major)
+//
+// Both read their operands in place (no transposed copies): the MN-major operands are
+// fetched as 64 x 64 TMA boxes and described to tcgen05.mma with the MN-major bit. d_weight
+// is accumulated over the whole batch in fp32 tensor memory and written once.
+#include "frx_host.cuh"
+
+namespace frx {
+
+// Writes the fp32 accumulator tile as bf16 or fp32 rows: each thread owns one output row and
+// stores 32 consecutive columns per TMEM load.
+struct StoreEpilogue {
+  struct Params {
+    void* out;
+    int64_t ld_out;
+    int rows;
+    int cols;
+    int out_f32;
+    int vec_ok;  // base and ld allow 16-byte vector stores
+  };
+
+  template <class Release>
+  __device__ __forceinline__ static void run(const Params& p, uint32_t tacc, int m_blk, int n_blk, int q, int lane,
+                                             Release release) {
+    const int row = m_blk * kBM + q * 32 + lane;
+    const int n0 = n_blk * kBN;
+    const int ncols = min(kBN, p.cols - n0);
+    const bool row_ok = row < p.rows;
+    float v[32];
+#pragma unroll 1
+    for (int c = 0; c < kBN / 32; ++c) {
+      const int lim = ncols - c * 32;
+      if (lim <= 0) break;
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after per-row branches
+      tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
+      if (!row_ok) continue;  // uniform reconvergence is restored by the __syncwarp above
+      const int64_t off = static_cast<int64_t>(row) * p.ld_out + n0 + c * 32;
+      if (p.out_f32) {
+        float* dst = static_cast<float*>(p.out) + off;
+        if (lim >= 32 && p.vec_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < lim) dst[j] = v[j];
+        }
+      } else {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + off;
+        if (lim >= 32 && p.vec_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 pk;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
+            pk.x = *reinterpret_cast<uint32_t*>(&h0);
+            pk.y = *reinterpret_cast<uint32_t*>(&h1);
+            pk.z = *reinterpret_cast<uint32_t*>(&h2);
+            pk.w = *reinterpret_cast<uint32_t*>(&h3);
+            *reinterpret_cast<uint4*>(dst + j) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < lim) dst[j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+    release();
+  }
+};
+
+static int check_out(void* out, int64_t ld, int64_t cols, int out_dtype, const char* who) {
+  FRX_REQUIRE(out != nullptr, FRX_ERR_INVALID_ARG, "%s: null output pointer", who);
+  FRX_REQUIRE(out_dtype == FRX_DTYPE_BF16 || out_dtype == FRX_DTYPE_F32, FRX_ERR_INVALID_ARG,
+              "%s: out_dtype must be FRX_DTYPE_BF16 or FRX_DTYPE_F32", who);
+  FRX_REQUIRE(ld >= cols, FRX_ERR_INVALID_ARG, "%s: output leading dimension %lld < %lld columns", who,
+              (long long)ld, (long long)cols);
+  return FRX_OK;
+}
+
+static StoreEpilogue::Params store_params(void* out, int64_t ld, int64_t rows, int64_t cols, int out_dtype) {
+  StoreEpilogue::Params ep;
+  ep.out = out;
+  ep.ld_out = ld;
+  ep.rows = static_cast<int>(rows);
+  ep.cols = static_cast<int>(cols);
+  ep.out_f32 = out_dtype == FRX_DTYPE_F32 ? 1 : 0;
+  const int64_t elem = ep.out_f32 ? 4 : 2;
+  ep.vec_ok = aligned16(out) && ((ld * elem) % 16 == 0) ? 1 : 0;
+  return ep;
+}
+
+}  // namespace frx
+
+extern "C" int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void* weight, int64_t ld_weight,
+                                void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows, int64_t hidden_dim,
+                                int64_t vocab_shard, int* status, void* stream) {
+  using namespace frx;
+  FRX_REQUIRE(rows >= 0 && hidden_dim >= 1 && vocab_shard >= 1 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
+                  vocab_shard < (1ll << 31),
+              FRX_ERR_INVALID_ARG, "frx_gemm_dhidden: bad sizes rows=%lld hidden_dim=%lld vocab_shard=%lld",
+              (long long)rows, (long long)hidden_dim, (long long)vocab_shard);
+  if (rows == 0) return FRX_OK;
+  FRX_REQUIRE(dlogits != nullptr && weight != nullptr, FRX_ERR_INVALID_ARG, "frx_gemm_dhidden: null input pointer");
+  int rc = check_out(d_hidden, ld_d_hidden, hidden_dim, out_dtype, "frx_gemm_dhidden");
+  if (rc) return rc;
+  Operand a{dlogits, ld_dlogits, rows, vocab_shard, false};  // [rows, V] row-major, K = V contiguous
+  Operand b{weight, ld_weight, hidden_dim, vocab_shard, true};  // [V, H] row-major, N = H contiguous
+  return launch_gemm<false, true, StoreEpilogue>(a, b, rows, hidden_dim, vocab_shard, 8,
+                                                 store_params(d_hidden, ld_d_hidden, rows, hidden_dim, out_dtype),
+                                                 status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
+                                void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
+                                int64_t hidden_dim, int64_t rows, int* status, void* stream) {
+  using namespace frx;
+  FRX_REQUIRE(rows >= 1 && hidden_dim >= 1 && vocab_shard >= 0 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
+                  vocab_shard < (1ll << 31),
+              FRX_ERR_INVALID_ARG, "frx_gemm_dweight: bad sizes rows=%lld hidden_dim=%lld vocab_shard=%lld",
+              (long long)rows, (long long)hidden_dim, (long long)vocab_shard);
+  if (vocab_shard == 0) return FRX_OK;
+  FRX_REQUIRE(dlogits != nullptr && hidden != nullptr, FRX_ERR_INVALID_ARG, "frx_gemm_dweight: null input pointer");
+  int rc = check_out(d_weight, ld_d_weight, hidden_dim, out_dtype, "frx_gemm_dweight");
+  if (rc) return rc;
+  Operand a{dlogits, ld_dlogits, vocab_shard, rows, true};  // [rows, V] row-major, M = V contiguous
+  Operand b{hidden, ld_hidden, hidden_dim, rows, true};     // [rows, H] row-major, N = H contiguous
+  return launch_gemm<true, true, StoreEpilogue>(a, b, vocab_shard, hidden_dim, rows, 8,
+                                                store_params(d_weight, ld_d_weight, vocab_shard, hidden_dim, out_dtype),
+                                                status, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,165 @@
+// Forward GEMM with the cross-entropy / entropy row reduction fused into its epilogue.
+//
+// Each finished 128 x 256 fp32 accumulator tile is read from tensor memory by the four
+// epilogue warps, one thread per row (TMEM lane == row), so the row statistics need no
+// shared memory and no shuffles. Two passes over the tile's TMEM columns:
+//   pass 1: tile max m (and the target logit when the row's target lies in the tile;
+//           optionally the fp32 logits are streamed out to HBM here),
+//   pass 2: s = sum exp(z - m) and u = sum (z - m) exp(z - m) against that exact tile max.
+// The reference computes the same four numbers per (row, 256-column tile) in
+// fast_reduction/gemm_ce_entropy_epilogue.py:184-271 (its third slot is sum z exp(z - m)).
+// Columns at or beyond the shard's vocabulary size are skipped, not sentinel-filled.
+#include "frx_host.cuh"
+
+namespace frx {
+
+// v[idx] for a runtime idx in [0, 32) as a 5-level select tree, so the array stays in
+// registers (an indexed read would demote it to local memory).
+__device__ __forceinline__ float select32(const float (&v)[32], int idx) {
+  float w16[16], w8[8], w4[4], w2[2];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) w16[j] = (idx & 16) ? v[j + 16] : v[j];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) w8[j] = (idx & 8) ? w16[j + 8] : w16[j];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) w4[j] = (idx & 4) ? w8[j + 4] : w8[j];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) w2[j] = (idx & 2) ? w4[j + 2] : w4[j];
+  return (idx & 1) ? w2[1] : w2[0];
+}
+
+struct CEPartialsEpilogue {
+  struct Params {
+    const int64_t* target;
+    int64_t vocab_offset;
+    int rows;
+    int vocab_shard;
+    float4* partials;
+    int64_t tile_stride;
+    float* logits;
+    int64_t ld_logits;
+  };
+
+  template <class Release>
+  __device__ __forceinline__ static void run(const Params& p, uint32_t tacc, int m_blk, int n_blk, int q,
+                                             int lane, Release release) {
+    // Row handled by this thread: TMEM lane (q * 32 + lane) of the tile.
+    const int row = m_blk * kBM + q * 32 + lane;
+    const int n0 = n_blk * kBN;
+    const int ncols = min(kBN, p.vocab_shard - n0);
+    const bool row_ok = row < p.rows;
+    int tcol = -1;
+    if (row_ok && p.target != nullptr) {
+      const long long lt = static_cast<long long>(p.target[row]) - p.vocab_offset - n0;
+      if (lt >= 0 && lt < ncols) tcol = static_cast<int>(lt);
+    }
+    float* lrow = (p.logits != nullptr && row_ok) ? p.logits + static_cast<int64_t>(row) * p.ld_logits + n0 : nullptr;
+    const bool lvec = lrow != nullptr && ((reinterpret_cast<uintptr_t>(lrow) & 15u) == 0);
+
+    float v[32];
+    float mx0 = -INFINITY, mx1 = -INFINITY, zt = 0.0f;
+#pragma unroll 1
+    for (int c = 0; c < kBN / 32; ++c) {
+      const int lim = ncols - c * 32;  // warp-uniform
+      if (lim <= 0) break;
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after per-row branches
+      tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
+      if (lim >= 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          mx0 = fmaxf(mx0, v[j]);
+          mx1 = fmaxf(mx1, v[j + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (j < lim) mx0 = fmaxf(mx0, v[j]);
+      }
+      if ((tcol >> 5) == c) zt = select32(v, tcol & 31);
+      if (lrow != nullptr) {
+        float* dst = lrow + c * 32;
+        if (lim >= 32 && lvec) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j < lim) dst[j] = v[j];
+        }
+      }
+    }
+    const float mx = fmaxf(mx0, mx1);
+    const float mx_l2 = mx * kLog2e;
+    float s0 = 0.f, s1 = 0.f, u0 = 0.f, u1 = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < kBN / 32; ++c) {
+      const int lim = ncols - c * 32;
+      if (lim <= 0) break;
+      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after per-row branches
+      tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
+      if (lim >= 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float e0 = ex2_approx(fmaf(v[j], kLog2e, -mx_l2));
+          const float e1 = ex2_approx(fmaf(v[j + 1], kLog2e, -mx_l2));
+          s0 += e0;
+          s1 += e1;
+          u0 = fmaf(v[j] - mx, e0, u0);
+          u1 = fmaf(v[j + 1] - mx, e1, u1);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (j < lim) {
+            const float e = ex2_approx(fmaf(v[j], kLog2e, -mx_l2));
+            s0 += e;
+            u0 = fmaf(v[j] - mx, e, u0);
+          }
+        }
+      }
+    }
+    release();  // accumulator buffer may now be overwritten by the next tile's MMAs
+    if (row_ok) p.partials[static_cast<int64_t>(n_blk) * p.tile_stride + row] = make_float4(mx, s0 + s1, u0 + u1, zt);
+  }
+};
+
+}  // namespace frx
+
+extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
+                                const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
+                                int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
+                                int64_t ld_logits, int* status, void* stream) {
+  using namespace frx;
+  FRX_REQUIRE(rows >= 0 && vocab_shard >= 1 && hidden_dim >= 1, FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials: bad sizes rows=%lld vocab_shard=%lld hidden_dim=%lld", (long long)rows,
+              (long long)vocab_shard, (long long)hidden_dim);
+  FRX_REQUIRE(rows < (1ll << 31) && vocab_shard < (1ll << 31) && hidden_dim < (1ll << 31), FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials: sizes must be below 2^31");
+  if (rows == 0) return FRX_OK;
+  FRX_REQUIRE(hidden != nullptr && weight != nullptr && partials != nullptr, FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials: null hidden/weight/partials pointer");
+  FRX_REQUIRE(hidden_dim % 8 == 0, FRX_ERR_UNSUPPORTED, "frx_fwd_partials: hidden_dim %lld must be a multiple of 8",
+              (long long)hidden_dim);
+  FRX_REQUIRE(tile_stride >= rows, FRX_ERR_INVALID_ARG, "frx_fwd_partials: tile_stride %lld < rows %lld",
+              (long long)tile_stride, (long long)rows);
+  FRX_REQUIRE((reinterpret_cast<uintptr_t>(partials) & 15u) == 0, FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials: partials must be 16-byte aligned");
+  FRX_REQUIRE(logits == nullptr || ld_logits >= vocab_shard, FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials: ld_logits %lld < vocab_shard %lld", (long long)ld_logits, (long long)vocab_shard);
+  CEPartialsEpilogue::Params ep;
+  ep.target = target;
+  ep.vocab_offset = vocab_offset;
+  ep.rows = static_cast<int>(rows);
+  ep.vocab_shard = static_cast<int>(vocab_shard);
+  ep.partials = reinterpret_cast<float4*>(partials);
+  ep.tile_stride = tile_stride;
+  ep.logits = logits;
+  ep.ld_logits = ld_logits;
+  Operand a{hidden, ld_hidden, rows, hidden_dim, false};
+  Operand b{weight, ld_weight, vocab_shard, hidden_dim, false};
+  // A band of up to 64 row blocks (8192 rows, 64 MiB of bf16 hidden at H=4096) stays in L2
+  // while the CTAs sweep the vocabulary.
+  return launch_gemm<false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, 64, ep, status,
+                                                       static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,229 @@
+// Persistent, warp-specialised tcgen05 GEMM core shared by every contraction of the engine:
+//
+//   D[m, n] = sum_k A[m, k] * B[n, k]     (bf16 operands, fp32 accumulation in TMEM)
+//
+// with a pluggable epilogue that consumes each finished 128 x 256 fp32 accumulator tile
+// straight from tensor memory (the forward CE/entropy reduction, a bf16/fp32 store, ...).
+//
+// CTA layout (192 threads, one CTA per SM):
+//   warp 0      TMA producer: streams 128x64 A and 256x64 B bf16 tiles into a 4-deep
+//               shared-memory ring (128-byte swizzle), completion counted on mbarriers.
+//   warp 1      MMA issuer: owns the 512-column TMEM allocation; one thread issues
+//               tcgen05.mma (M=128, N=256, K=16) into one of two 256-column accumulators,
+//               so the epilogue of tile i overlaps the mainloop of tile i+1.
+//   warps 2..5  epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32), i.e. one thread
+//               per output row, and runs Epi::run on the tile.
+//
+// Operands may be K-major (row-major [rows, K], one 64-element box per tile row) or
+// MN-major (row-major [K, rows], 64x64 boxes side by side), selected per operand at compile
+// time; this is how the backward GEMMs read dlogits / weight / hidden in place without any
+// transpose copies.
+#pragma once
+
+#include "frx_ptx.cuh"
+
+namespace frx {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
+constexpr int kBBytes = kBN * kBK * 2;  // 32 KiB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kMNBoxBytes = 64 * kBK * 2;  // one 64 (MN) x 64 (K) bf16 box, 8 KiB
+constexpr int kGemmSmemBytes = kStages * kStageBytes + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+
+// Grouped rasterisation over (m-block, n-block) tiles: tiles are taken in bands of `group`
+// m-blocks; inside a band the m-block index runs fastest. Concurrently resident CTAs then
+// share both the band's A rows and a narrow slice of B in L2.
+struct TileSched {
+  int num_m;
+  int num_n;
+  int group;
+  int num_tiles;
+  __device__ __forceinline__ void get(int t, int& m_blk, int& n_blk) const {
+    const int per_band = group * num_n;
+    const int band = t / per_band;
+    const int r = t - band * per_band;
+    const int first_m = band * group;
+    const int gm = min(group, num_m - first_m);
+    n_blk = r / gm;
+    m_blk = first_m + (r - n_blk * gm);
+  }
+};
+
+template <bool kAMN, bool kBMN, class Epi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        TileSched sched, int num_k_blocks, typename Epi::Params ep, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + kStages * kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_b + kStages * kBBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < sched.num_tiles && ok; t += gridDim.x) {
+        int m_blk, n_blk;
+        sched.get(t, m_blk, n_blk);
+        const int m0 = m_blk * kBM;
+        const int n0 = n_blk * kBN;
+        for (int kb = 0; kb < num_k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], kStageBytes);
+          const int k0 = kb * kBK;
+          uint8_t* da = s_a + stage * kABytes;
+          uint8_t* db = s_b + stage * kBBytes;
+          if (kAMN) {
+#pragma unroll
+            for (int g = 0; g < kBM / 64; ++g) tma_load_2d(da + g * kMNBoxBytes, &tm_a, &full[stage], m0 + 64 * g, k0);
+          } else {
+            tma_load_2d(da, &tm_a, &full[stage], k0, m0);
+          }
+          if (kBMN) {
+#pragma unroll
+            for (int g = 0; g < kBN / 64; ++g) tma_load_2d(db + g * kMNBoxBytes, &tm_b, &full[stage], n0 + 64 * g, k0);
+          } else {
+            tma_load_2d(db, &tm_b, &full[stage], k0, n0);
+          }
+          ++issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every copy still in flight land before the CTA's shared memory goes away.
+        const long long first = issued > kStages ? issued - kStages : 0;
+        for (long long j = first; j < issued; ++j)
+          mbar_wait_drain(&full[j % kStages], static_cast<uint32_t>((j / kStages) & 1), status);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, kBN, kAMN, kBMN);
+      constexpr uint32_t a_lbo = kAMN ? kMNBoxBytes : 16;
+      constexpr uint32_t b_lbo = kBMN ? kMNBoxBytes : 16;
+      constexpr uint32_t a_kstep = kAMN ? 16 * 128 : 32;  // bytes per UMMA_K (=16) step
+      constexpr uint32_t b_kstep = kBMN ? 16 * 128 : 32;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < sched.num_tiles && ok; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBN);
+        for (int kb = 0; kb < num_k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(s_a + stage * kABytes);
+          const uint32_t b_addr = smem_u32(s_b + stage * kBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t adesc = make_smem_desc_sw128(a_addr + k * a_kstep, a_lbo, 1024);
+            const uint64_t bdesc = make_smem_desc_sw128(b_addr + k * b_kstep, b_lbo, 1024);
+            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);  // frees this smem slot once the MMAs have read it
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      // All MMAs issued by this thread must finish before TMEM is released.
+      umma_commit(mma_done);
+      mbar_wait_drain(mma_done, 0, status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue warps
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < sched.num_tiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      int ok = 1;
+      if (lane == 0)
+        ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, status, kStatusTimeoutEpilogue) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int m_blk, n_blk;
+      sched.get(t, m_blk, n_blk);
+      const uint32_t tacc = tmem_base + static_cast<uint32_t>(buf * kBN) + (static_cast<uint32_t>(q * 32) << 16);
+      Epi::run(ep, tacc, m_blk, n_blk, q, lane, [&]() {
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+      });
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace frx

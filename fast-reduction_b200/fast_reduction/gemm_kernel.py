@@ -1,0 +1,283 @@
+"""Drop-in for `fast_reduction.gemm_kernel` (reference: fast_reduction/gemm_kernel.py), B200 engine.
+
+Public functions keep the reference's names, signatures and return conventions:
+
+  gemm_fused_ce_entropy(hidden_states, weight, target, bias=None, chunk_size=4096, tile_M=128, tile_N=256)
+      -> (ce_loss, entropy, log_probs), fp32, shaped like hidden_states.shape[:-1]
+      (reference gemm_kernel.py:276-356)
+  gemm_megakernel_fast(hidden_states, weight, target, bias=None, chunk_size=4096, ce_weight=1.0, ent_weight=-1.0)
+      -> (loss, ce_loss, entropy); loss is a 0-d tensor that requires grad, loss.backward() fills
+      hidden.grad / weight.grad (reference gemm_kernel.py:883-934)
+
+Engine (all device work is libfrx, sm_100a):
+  forward   frx_fwd_partials: tcgen05 GEMM whose epilogue reduces each 128x256 fp32 TMEM tile to
+            per-row softmax partials; logits never reach HBM.  frx_finalize: partials -> ce/H/lse.
+  training  the same GEMM also streams fp32 logits of one row chunk to HBM; frx_dlogits turns
+            them into bf16 dlogits for all rows; frx_gemm_dhidden / frx_gemm_dweight run once
+            over the full batch (d_weight accumulates over every row in TMEM: no fp32 d_weight
+            read-modify-write per chunk, no transposed weight copy).
+
+Semantics chosen where the reference is inconsistent (documented in DESIGN.md):
+  * ignore_index (default -100): ce = 0, log_probs = 0 and no CE gradient for such rows; the
+    entropy and its gradient are kept (torch nll_loss semantics, reference baseline.py:80).
+  * bias: the reference accepts it but never adds it to the logits (gemm_kernel.py:280);
+    here a non-None bias raises NotImplementedError.
+  * loss = ce_weight * sum(ce) + ent_weight * sum(entropy) (a sum, gemm_kernel.py:897).
+  * tile_M / tile_N are accepted for signature compatibility and ignored (tiles are fixed at
+    128 x 256 by the sm_100a kernel; the partials use 256-column vocabulary tiles).
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from . import ops
+
+IGNORE_INDEX = -100
+
+
+def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Optional[Tensor]):
+    if bias is not None:
+        raise NotImplementedError("bias is not supported by the B200 engine (the reference ignores it in the forward)")
+    if hidden_states.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise NotImplementedError(
+            f"the B200 engine computes in bf16; got hidden {hidden_states.dtype}, weight {weight.dtype}"
+        )
+    if weight.dim() != 2:
+        raise ValueError(f"weight must be [V, H], got shape {tuple(weight.shape)}")
+    H = hidden_states.shape[-1]
+    if weight.shape[1] != H:
+        raise ValueError(f"hidden size mismatch: hidden [..., {H}] vs weight {tuple(weight.shape)}")
+    if H % 8 != 0:
+        raise NotImplementedError(f"hidden size must be a multiple of 8 (TMA row alignment), got {H}")
+    batch_shape = hidden_states.shape[:-1]
+    hidden_2d = hidden_states.reshape(-1, H)
+    if hidden_2d.stride(1) != 1 or hidden_2d.stride(0) % 8 != 0 or hidden_2d.data_ptr() % 16 != 0:
+        hidden_2d = hidden_2d.contiguous()
+    if weight.stride(1) != 1 or weight.stride(0) % 8 != 0 or weight.data_ptr() % 16 != 0:
+        weight = weight.contiguous()
+    target_1d = target.reshape(-1)
+    if target_1d.numel() != hidden_2d.shape[0]:
+        raise ValueError(f"target has {target_1d.numel()} elements, expected {hidden_2d.shape[0]}")
+    if target_1d.dtype != torch.int64:
+        if target_1d.dtype.is_floating_point or target_1d.dtype == torch.bool:
+            raise TypeError(f"target must be an integer tensor, got {target_1d.dtype}")
+        target_1d = target_1d.to(torch.int64)
+    target_1d = target_1d.contiguous()
+    ops._require_cuda(hidden_2d, weight, target_1d)
+    return batch_shape, hidden_2d, weight, target_1d
+
+
+def _chunk_rows(chunk_size: int, B: int) -> int:
+    if chunk_size is None or chunk_size <= 0:
+        raise ValueError(f"chunk_size must be positive, got {chunk_size}")
+    return max(1, min(int(chunk_size), B))
+
+
+def forward_stats(
+    hidden_2d: Tensor,
+    weight: Tensor,
+    target_1d: Tensor,
+    chunk_size: int,
+    *,
+    vocab_offset: int = 0,
+    ce: Optional[Tensor] = None,
+    entropy: Optional[Tensor] = None,
+    lse: Optional[Tensor] = None,
+    log_probs: Optional[Tensor] = None,
+    merged: Optional[Tensor] = None,
+    vocab_size: Optional[int] = None,
+    ignore_index: int = IGNORE_INDEX,
+) -> None:
+    """Forward over one vocabulary shard, chunked over rows: GEMM-epilogue partials + finalize.
+
+    Writes whichever of ce / entropy / lse / log_probs / merged ([B, 4] (M, S, U, ZT) per row,
+    for a later cross-shard merge) are given.
+    """
+    B = hidden_2d.shape[0]
+    V = weight.shape[0]
+    if B == 0:
+        return
+    T = ops.n_vocab_tiles(V)
+    chunk = _chunk_rows(chunk_size, B)
+    partials = torch.empty(T, chunk, 4, device=hidden_2d.device, dtype=torch.float32)
+    vocab_size = V if vocab_size is None else vocab_size
+    for start in range(0, B, chunk):
+        end = min(start + chunk, B)
+        rows = end - start
+        ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset)
+        ops.finalize(
+            partials, T, rows, chunk,
+            target=target_1d[start:end], vocab_size=vocab_size, ignore_index=ignore_index,
+            ce=None if ce is None else ce[start:end],
+            entropy=None if entropy is None else entropy[start:end],
+            lse=None if lse is None else lse[start:end],
+            log_probs=None if log_probs is None else log_probs[start:end],
+            merged=None if merged is None else merged[start:end],
+        )
+
+
+def gemm_fused_ce_entropy(
+    hidden_states: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    bias: Optional[Tensor] = None,
+    chunk_size: int = 4096,
+    tile_M: int = 128,
+    tile_N: int = 256,
+    ignore_index: int = IGNORE_INDEX,
+) -> Tuple[Tensor, Tensor, Tensor]:
+    """Fused linear + CE + entropy forward. Returns (ce_loss, entropy, log_probs), each fp32
+    and shaped like ``hidden_states.shape[:-1]``. The [chunk, V] logits never reach HBM."""
+    batch_shape, hidden_2d, weight, target_1d = _prepare(hidden_states, weight, target, bias)
+    B = hidden_2d.shape[0]
+    dev = hidden_2d.device
+    ce = torch.empty(B, device=dev, dtype=torch.float32)
+    ent = torch.empty(B, device=dev, dtype=torch.float32)
+    logp = torch.empty(B, device=dev, dtype=torch.float32)
+    forward_stats(hidden_2d, weight, target_1d, chunk_size, ce=ce, entropy=ent, log_probs=logp,
+                  ignore_index=ignore_index)
+    return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
+
+
+# The reference's two-pass epilogue variant (Level 5.2, gemm_kernel.py:363-534) exists for
+# precision: no online merge inside a CTA tile. The sm_100a epilogue already reduces each
+# 256-column tile in two passes against the exact tile max, so both names run the same engine.
+gemm_fused_ce_entropy_v2 = gemm_fused_ce_entropy
+
+
+def fwd_bwd_shard(
+    hidden_2d: Tensor,
+    weight: Tensor,
+    target_1d: Tensor,
+    chunk_size: int,
+    ce_weight: float,
+    ent_weight: float,
+    *,
+    lse: Tensor,
+    entropy: Tensor,
+    vocab_offset: int = 0,
+    ignore_index: int = IGNORE_INDEX,
+    stats_fn=None,
+    g_ce: Optional[Tensor] = None,
+    g_ent: Optional[Tensor] = None,
+    dhidden_fp32: bool = False,
+    dhidden_hook=None,
+):
+    """Training pass over one vocabulary shard; returns (d_hidden [B, H], d_weight [V_shard, H], pending)
+    where d_hidden is this shard's contribution (fp32 if ``dhidden_fp32``) and ``pending`` is what
+    ``dhidden_hook(d_hidden)`` returned (it runs between the d_hidden and d_weight GEMMs, so a
+    cross-shard reduction can overlap the d_weight GEMM), or None.
+
+    For each row chunk: GEMM epilogue writes the chunk's fp32 logits (and partials); the
+    per-row lse / entropy of the chunk are produced by ``stats_fn(start, end, partials, T, chunk)``
+    (single GPU: a local finalize; vocabulary-parallel: local merge + cross-rank exchange);
+    frx_dlogits writes bf16 dlogits of the chunk into a [B, V_shard] buffer. Then one
+    d_hidden GEMM and one d_weight GEMM over all rows.
+    """
+    B, H = hidden_2d.shape
+    V = weight.shape[0]
+    dev = hidden_2d.device
+    chunk = _chunk_rows(chunk_size, B)
+    T = ops.n_vocab_tiles(V)
+    partials = torch.empty(T, chunk, 4, device=dev, dtype=torch.float32)
+    logits = torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32)
+    dz = torch.empty(B, ops.round_up(V, 8), device=dev, dtype=torch.bfloat16)
+    for start in range(0, B, chunk):
+        end = min(start + chunk, B)
+        rows = end - start
+        ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
+                         logits=logits)
+        stats_fn(start, end, partials, T, chunk)
+        ops.dlogits(
+            logits, target_1d[start:end], lse[start:end], entropy[start:end], dz[start:end],
+            rows=rows, vocab_shard=V, ce_weight=ce_weight, ent_weight=ent_weight,
+            g_ce=None if g_ce is None else g_ce[start:end],
+            g_ent=None if g_ent is None else g_ent[start:end],
+            vocab_offset=vocab_offset, ignore_index=ignore_index,
+        )
+    del logits, partials
+    d_hidden = torch.empty(B, H, device=dev, dtype=torch.float32 if dhidden_fp32 else hidden_2d.dtype)
+    ops.gemm_dhidden(dz, weight, d_hidden, rows=B, vocab_shard=V)
+    pending = dhidden_hook(d_hidden) if dhidden_hook is not None else None
+    d_weight = torch.empty(V, H, device=dev, dtype=weight.dtype)
+    ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
+    return d_hidden, d_weight, pending
+
+
+def _megakernel_fwd_bwd(hidden_2d, weight, target_1d, chunk_size, ce_weight, ent_weight, ignore_index):
+    B = hidden_2d.shape[0]
+    V = weight.shape[0]
+    dev = hidden_2d.device
+    ce = torch.empty(B, device=dev, dtype=torch.float32)
+    ent = torch.empty(B, device=dev, dtype=torch.float32)
+    lse = torch.empty(B, device=dev, dtype=torch.float32)
+    if B == 0:
+        return ce, ent, torch.zeros_like(hidden_2d), torch.zeros_like(weight)
+
+    def local_stats(start, end, partials, T, chunk):
+        ops.finalize(
+            partials, T, end - start, chunk, target=target_1d[start:end], vocab_size=V, ignore_index=ignore_index,
+            ce=ce[start:end], entropy=ent[start:end], lse=lse[start:end],
+        )
+
+    d_hidden, d_weight, _ = fwd_bwd_shard(
+        hidden_2d, weight, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
+        ignore_index=ignore_index, stats_fn=local_stats,
+    )
+    return ce, ent, d_hidden, d_weight
+
+
+def _scale_grads(d_hidden: Tensor, d_weight: Tensor, dloss: Tensor):
+    # loss.backward() without an explicit gradient passes exactly 1.0: return the stored
+    # gradients without another full pass over them.
+    if dloss.numel() == 1 and float(dloss) == 1.0:
+        return d_hidden, d_weight
+    return d_hidden * dloss, d_weight * dloss
+
+
+class GemmMegakernel(torch.autograd.Function):
+    """Training op: all gradient work runs in forward; backward only scales by dloss
+    (reference GemmMegakernel, gemm_kernel.py:883-913)."""
+
+    @staticmethod
+    def forward(ctx, hidden_states, weight, target, bias, chunk_size, ce_weight, ent_weight):
+        batch_shape, hidden_2d, weight_c, target_1d = _prepare(hidden_states, weight, target, bias)
+        ce, ent, d_hidden, d_weight = _megakernel_fwd_bwd(
+            hidden_2d, weight_c, target_1d, chunk_size, float(ce_weight), float(ent_weight), IGNORE_INDEX,
+        )
+        loss = ce_weight * ce.sum() + ent_weight * ent.sum()
+        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight)
+        ce = ce.view(batch_shape)
+        ent = ent.view(batch_shape)
+        ctx.mark_non_differentiable(ce, ent)
+        return loss, ce, ent
+
+    @staticmethod
+    def backward(ctx, dloss, _g_ce, _g_ent):
+        d_hidden, d_weight = ctx.saved_tensors
+        d_hidden, d_weight = _scale_grads(d_hidden, d_weight, dloss)
+        return d_hidden, d_weight, None, None, None, None, None
+
+
+def gemm_megakernel_fast(
+    hidden_states: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    bias: Optional[Tensor] = None,
+    chunk_size: int = 4096,
+    ce_weight: float = 1.0,
+    ent_weight: float = -1.0,
+) -> Tuple[Tensor, Tensor, Tensor]:
+    """Training megakernel. Returns (loss, ce_loss, entropy): loss is a scalar that requires
+    grad; ce_loss and entropy are per-row and detached."""
+    return GemmMegakernel.apply(hidden_states, weight, target, bias, chunk_size, ce_weight, ent_weight)
+
+
+# The reference's Level-5 "fast" variant (gemm_kernel.py:713-764) has the same contract as the
+# megakernel (gradients precomputed in forward, backward scales by dloss); here both names run
+# the same sm_100a training path.
+gemm_fused_ce_entropy_fast = gemm_megakernel_fast

@@ -1,0 +1,233 @@
+"""Tensor-level wrappers over the libfrx C ABI (one function per entry point).
+
+These functions take torch tensors, validate them, and pass raw device pointers plus sizes
+to libfrx on the tensors' current CUDA stream. Outputs are written into caller-provided
+tensors, as in the reference's custom ops (`mutates_args`, e.g.
+fast_reduction/gemm_ce_entropy_finalize.py:123-148, cute_dlogits.py:121-159).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _native as nat
+
+VOCAB_TILE = nat.FRX_VOCAB_TILE
+# Never equal to a real target id: disables the ignore_index rule.
+NO_IGNORE = -(2**63)
+
+# Optional launch observer (used by bench.py to time each libfrx kernel with CUDA events on the
+# launching stream): an object with before(name, device) / after(name, device), or None.
+_observer = None
+
+
+def set_launch_observer(observer):
+    """Installs `observer` (or None) and returns the previous one."""
+    global _observer
+    prev, _observer = _observer, observer
+    return prev
+
+
+def _launch(name: str, dev: torch.device, call) -> int:
+    obs = _observer
+    if obs is None:
+        return call()
+    obs.before(name, dev)
+    rc = call()
+    obs.after(name, dev)
+    return rc
+
+
+def n_vocab_tiles(vocab_shard: int) -> int:
+    return (vocab_shard + VOCAB_TILE - 1) // VOCAB_TILE
+
+
+def round_up(x: int, m: int) -> int:
+    return (x + m - 1) // m * m
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("fast_reduction (B200 engine) requires CUDA tensors; got a tensor on " + str(t.device))
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"all tensors must be on one device, got {dev} and {t.device}")
+    return dev
+
+
+def _row_major(t: torch.Tensor, name: str) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"{name} must be a 2-D tensor with unit column stride, got shape {tuple(t.shape)} "
+                         f"stride {t.stride()}")
+    return t.stride(0)
+
+
+def fwd_partials(
+    hidden: torch.Tensor,
+    weight: torch.Tensor,
+    target: torch.Tensor | None,
+    partials: torch.Tensor,
+    tile_stride: int,
+    vocab_offset: int = 0,
+    logits: torch.Tensor | None = None,
+) -> None:
+    """partials[t, r] <- (m, s, u, zt) of z = hidden @ weight.T over vocab tile t (see include/frx.h)."""
+    dev = _require_cuda(hidden, weight, target, partials, logits)
+    ldh = _row_major(hidden, "hidden")
+    ldw = _row_major(weight, "weight")
+    rows, hdim = hidden.shape
+    vshard = weight.shape[0]
+    if weight.shape[1] != hdim:
+        raise ValueError(f"hidden dim mismatch: hidden {tuple(hidden.shape)} vs weight {tuple(weight.shape)}")
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("hidden and weight must be bfloat16")
+    if target is not None and (target.dtype != torch.int64 or not target.is_contiguous() or target.numel() < rows):
+        raise ValueError("target must be a contiguous int64 tensor with one id per row")
+    if partials.dtype != torch.float32 or not partials.is_contiguous():
+        raise ValueError("partials must be contiguous float32")
+    if partials.numel() < 4 * n_vocab_tiles(vshard) * tile_stride:
+        raise ValueError("partials buffer too small")
+    ldl = 0
+    if logits is not None:
+        ldl = _row_major(logits, "logits")
+        if logits.dtype != torch.float32 or logits.shape[0] < rows or logits.shape[1] < vshard:
+            raise ValueError("logits must be float32 [rows, >= vocab_shard]")
+    lib = nat.load()
+    rc = _launch("fwd_partials", dev, lambda: lib.frx_fwd_partials(
+        hidden.data_ptr(), ldh, weight.data_ptr(), ldw, nat.ptr(target), rows, vshard, hdim, vocab_offset,
+        partials.data_ptr(), tile_stride, nat.ptr(logits), ldl, nat.status_word(dev).data_ptr(), nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_fwd_partials")
+
+
+def finalize(
+    partials: torch.Tensor,
+    n_tiles: int,
+    rows: int,
+    tile_stride: int,
+    *,
+    ref_layout: bool = False,
+    target: torch.Tensor | None = None,
+    vocab_size: int = 0,
+    ignore_index: int = NO_IGNORE,
+    ce: torch.Tensor | None = None,
+    entropy: torch.Tensor | None = None,
+    lse: torch.Tensor | None = None,
+    log_probs: torch.Tensor | None = None,
+    merged: torch.Tensor | None = None,
+) -> None:
+    """Merges [n_tiles, tile_stride] float4 partials into per-row outputs (any may be None)."""
+    dev = _require_cuda(partials, target, ce, entropy, lse, log_probs, merged)
+    if partials.dtype != torch.float32 or not partials.is_contiguous():
+        raise ValueError("partials must be contiguous float32")
+    if partials.numel() < 4 * n_tiles * tile_stride or tile_stride < rows:
+        raise ValueError("partials buffer smaller than n_tiles * tile_stride float4")
+    for name, t in (("ce", ce), ("entropy", entropy), ("lse", lse), ("log_probs", log_probs)):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < rows):
+            raise ValueError(f"{name} must be contiguous float32 with >= rows elements")
+    if merged is not None and (merged.dtype != torch.float32 or not merged.is_contiguous() or merged.numel() < 4 * rows):
+        raise ValueError("merged must be contiguous float32 [rows, 4]")
+    if target is not None and (target.dtype != torch.int64 or not target.is_contiguous() or target.numel() < rows):
+        raise ValueError("target must be a contiguous int64 tensor with one id per row")
+    lib = nat.load()
+    rc = _launch("finalize", dev, lambda: lib.frx_finalize(
+        partials.data_ptr(), n_tiles, rows, tile_stride, nat.FRX_PARTIALS_REF_LAYOUT if ref_layout else 0,
+        nat.ptr(target), vocab_size, ignore_index, nat.ptr(ce), nat.ptr(entropy), nat.ptr(lse), nat.ptr(log_probs),
+        nat.ptr(merged), nat.status_word(dev).data_ptr(), nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_finalize")
+
+
+def dlogits(
+    logits: torch.Tensor,
+    target: torch.Tensor | None,
+    lse: torch.Tensor,
+    entropy: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    rows: int,
+    vocab_shard: int,
+    g_ce: torch.Tensor | None = None,
+    g_ent: torch.Tensor | None = None,
+    ce_weight: float = 1.0,
+    ent_weight: float = -1.0,
+    vocab_offset: int = 0,
+    ignore_index: int = NO_IGNORE,
+) -> None:
+    """out[r, j] <- d(sum g_ce*ce + g_ent*H)/dz[r, j] from fp32 logits (bf16 or fp32 out)."""
+    dev = _require_cuda(logits, target, lse, entropy, out, g_ce, g_ent)
+    ldl = _row_major(logits, "logits")
+    ldo = _row_major(out, "dlogits")
+    if logits.dtype != torch.float32:
+        raise TypeError("logits must be float32")
+    if out.dtype == torch.bfloat16:
+        odt = nat.FRX_DTYPE_BF16
+    elif out.dtype == torch.float32:
+        odt = nat.FRX_DTYPE_F32
+    else:
+        raise TypeError("dlogits output must be bfloat16 or float32")
+    if logits.shape[0] < rows or out.shape[0] < rows or logits.shape[1] < vocab_shard or out.shape[1] < vocab_shard:
+        raise ValueError("logits/out smaller than [rows, vocab_shard]")
+    for name, t in (("lse", lse), ("entropy", entropy), ("g_ce", g_ce), ("g_ent", g_ent)):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < rows):
+            raise ValueError(f"{name} must be contiguous float32 with >= rows elements")
+    if target is not None and (target.dtype != torch.int64 or not target.is_contiguous() or target.numel() < rows):
+        raise ValueError("target must be a contiguous int64 tensor with one id per row")
+    lib = nat.load()
+    rc = _launch("dlogits", dev, lambda: lib.frx_dlogits(
+        logits.data_ptr(), ldl, nat.ptr(target), lse.data_ptr(), entropy.data_ptr(), nat.ptr(g_ce), nat.ptr(g_ent),
+        float(ce_weight), float(ent_weight), out.data_ptr(), ldo, odt, rows, vocab_shard, vocab_offset, ignore_index,
+        nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_dlogits")
+
+
+def _out_dtype(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return nat.FRX_DTYPE_BF16
+    if t.dtype == torch.float32:
+        return nat.FRX_DTYPE_F32
+    raise TypeError("GEMM output must be bfloat16 or float32")
+
+
+def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int) -> None:
+    """out[rows, H] <- dz[rows, vocab_shard] @ weight[vocab_shard, H]."""
+    dev = _require_cuda(dz, weight, out)
+    if dz.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("dz and weight must be bfloat16")
+    ldz = _row_major(dz, "dz")
+    ldw = _row_major(weight, "weight")
+    ldo = _row_major(out, "d_hidden")
+    hdim = weight.shape[1]
+    if out.shape[0] < rows or out.shape[1] < hdim or weight.shape[0] < vocab_shard or dz.shape[1] < vocab_shard:
+        raise ValueError("shape mismatch in gemm_dhidden")
+    lib = nat.load()
+    rc = _launch("gemm_dhidden", dev, lambda: lib.frx_gemm_dhidden(
+        dz.data_ptr(), ldz, weight.data_ptr(), ldw, out.data_ptr(), ldo, _out_dtype(out), rows, hdim, vocab_shard,
+        nat.status_word(dev).data_ptr(), nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_gemm_dhidden")
+
+
+def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int) -> None:
+    """out[vocab_shard, H] <- dz[rows, vocab_shard]^T @ hidden[rows, H]."""
+    dev = _require_cuda(dz, hidden, out)
+    if dz.dtype != torch.bfloat16 or hidden.dtype != torch.bfloat16:
+        raise TypeError("dz and hidden must be bfloat16")
+    ldz = _row_major(dz, "dz")
+    ldh = _row_major(hidden, "hidden")
+    ldo = _row_major(out, "d_weight")
+    hdim = hidden.shape[1]
+    if out.shape[0] < vocab_shard or out.shape[1] < hdim or hidden.shape[0] < rows or dz.shape[0] < rows:
+        raise ValueError("shape mismatch in gemm_dweight")
+    lib = nat.load()
+    rc = _launch("gemm_dweight", dev, lambda: lib.frx_gemm_dweight(
+        dz.data_ptr(), ldz, hidden.data_ptr(), ldh, out.data_ptr(), ldo, _out_dtype(out), vocab_shard, hdim, rows,
+        nat.status_word(dev).data_ptr(), nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_gemm_dweight")

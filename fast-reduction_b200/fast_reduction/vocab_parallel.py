@@ -1,0 +1,177 @@
+"""Vocabulary-parallel fused linear + CE + entropy over the GPUs of one node.
+
+Each rank owns a contiguous slice [vocab_start, vocab_start + V_r) of the vocabulary (its rows
+of the weight) and the full hidden states and targets. The forward exchanges only per-row
+merged softmax statistics: every rank reduces its slice to (M, S, U, ZT) per row with the
+fused GEMM epilogue + a local merge, all-gathers the [B, 4] fp32 rows (16 bytes per row per
+rank) and merges them with the same associative rule as the per-tile merge
+(reference merge: fast_reduction/gemm_ce_entropy_finalize.py:78-92). Every rank then holds the
+full ce / entropy / lse.
+
+Training: dlogits and d_weight of a slice are local; d_hidden is a sum over slices, so each rank
+computes its partial d_hidden in fp32 and one all-reduce (on a side stream, overlapped with the
+d_weight GEMM) completes it.
+
+The reference is single-GPU; this module adds the sharded path around the same libfrx kernels.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from . import gemm_kernel as gk
+from . import ops
+
+
+def shard_bounds(vocab_size: int, world_size: int, rank: int) -> Tuple[int, int]:
+    """[start, end) of `rank`'s vocabulary slice: an even split, the remainder spread over the
+    first ranks (shards need not be multiples of the 256-column tile)."""
+    if world_size < 1 or not (0 <= rank < world_size):
+        raise ValueError(f"bad rank {rank} for world size {world_size}")
+    base, rem = divmod(vocab_size, world_size)
+    start = rank * base + min(rank, rem)
+    return start, start + base + (1 if rank < rem else 0)
+
+
+def merge_rows(merged_all: Tensor, target_1d: Tensor, vocab_size: int, ignore_index: int,
+               ce: Optional[Tensor] = None, entropy: Optional[Tensor] = None, lse: Optional[Tensor] = None,
+               log_probs: Optional[Tensor] = None) -> None:
+    """[world, B, 4] gathered per-shard statistics -> per-row outputs (frx_finalize over shards)."""
+    world, B, _ = merged_all.shape
+    ops.finalize(merged_all, world, B, B, target=target_1d, vocab_size=vocab_size, ignore_index=ignore_index,
+                 ce=ce, entropy=entropy, lse=lse, log_probs=log_probs)
+
+
+def _gather_stats(local: Tensor, group) -> Tensor:
+    world = dist.get_world_size(group)
+    out = torch.empty((world,) + tuple(local.shape), device=local.device, dtype=local.dtype)
+    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    return out
+
+
+def vocab_parallel_ce_entropy(
+    hidden_states: Tensor,
+    weight_shard: Tensor,
+    target: Tensor,
+    vocab_start: int,
+    vocab_size: int,
+    group=None,
+    chunk_size: int = 4096,
+    ignore_index: int = gk.IGNORE_INDEX,
+) -> Tuple[Tensor, Tensor, Tensor]:
+    """Forward over this rank's vocabulary slice; returns the full (ce_loss, entropy, log_probs)
+    (identical on every rank), shaped like hidden_states.shape[:-1]."""
+    batch_shape, hidden_2d, weight_shard, target_1d = gk._prepare(hidden_states, weight_shard, target, None)
+    B = hidden_2d.shape[0]
+    dev = hidden_2d.device
+    local = torch.empty(B, 4, device=dev, dtype=torch.float32)
+    gk.forward_stats(hidden_2d, weight_shard, target_1d, chunk_size, vocab_offset=vocab_start, merged=local,
+                     vocab_size=vocab_size, ignore_index=ignore_index)
+    gathered = _gather_stats(local, group)
+    ce = torch.empty(B, device=dev, dtype=torch.float32)
+    ent = torch.empty(B, device=dev, dtype=torch.float32)
+    logp = torch.empty(B, device=dev, dtype=torch.float32)
+    merge_rows(gathered, target_1d, vocab_size, ignore_index, ce=ce, entropy=ent, log_probs=logp)
+    return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
+
+
+def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, vocab_size, group, chunk_size,
+                            ce_weight, ent_weight, ignore_index):
+    B, H = hidden_2d.shape
+    dev = hidden_2d.device
+    ce = torch.empty(B, device=dev, dtype=torch.float32)
+    ent = torch.empty(B, device=dev, dtype=torch.float32)
+    lse = torch.empty(B, device=dev, dtype=torch.float32)
+    local = torch.empty(B, 4, device=dev, dtype=torch.float32)
+    Vr = weight_shard.shape[0]
+
+    def exchange_stats(start, end, partials, T, chunk):
+        rows = end - start
+        ops.finalize(partials, T, rows, chunk, merged=local[start:end])
+        gathered = _gather_stats(local[start:end], group)
+        merge_rows(gathered, target_1d[start:end], vocab_size, ignore_index, ce=ce[start:end],
+                   entropy=ent[start:end], lse=lse[start:end])
+
+    if Vr == 0:
+        raise ValueError("every rank needs a non-empty vocabulary slice")
+    d_hidden_f32, d_weight, pending = gk.fwd_bwd_shard(
+        hidden_2d, weight_shard, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
+        vocab_offset=vocab_start, ignore_index=ignore_index, stats_fn=exchange_stats, dhidden_fp32=True,
+        dhidden_hook=lambda dh: _allreduce_async(dh, group),
+    )
+    pending.wait_into_current()
+    return ce, ent, d_hidden_f32.to(hidden_2d.dtype), d_weight
+
+
+class _PendingAllReduce:
+    def __init__(self, event: torch.cuda.Event):
+        self.event = event
+
+    def wait_into_current(self):
+        torch.cuda.current_stream().wait_event(self.event)
+
+
+_side_streams: dict[int, torch.cuda.Stream] = {}
+
+
+def _allreduce_async(t: Tensor, group) -> _PendingAllReduce:
+    """All-reduce `t` (SUM) on a side stream, so the caller's next kernel (the d_weight GEMM)
+    overlaps the NVLink transfer; returns a handle whose wait orders the caller's stream after it."""
+    dev = t.device.index
+    side = _side_streams.get(dev)
+    if side is None:
+        side = torch.cuda.Stream(device=t.device)
+        _side_streams[dev] = side
+    main = torch.cuda.current_stream()
+    side.wait_stream(main)
+    with torch.cuda.stream(side):
+        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
+        done = torch.cuda.Event()
+        done.record(side)
+    t.record_stream(side)
+    return _PendingAllReduce(done)
+
+
+class VocabParallelMegakernel(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, hidden_states, weight_shard, target, vocab_start, vocab_size, group, chunk_size, ce_weight,
+                ent_weight):
+        batch_shape, hidden_2d, weight_c, target_1d = gk._prepare(hidden_states, weight_shard, target, None)
+        ce, ent, d_hidden, d_weight = _fwd_bwd_vocab_parallel(
+            hidden_2d, weight_c, target_1d, vocab_start, vocab_size, group, chunk_size, float(ce_weight),
+            float(ent_weight), gk.IGNORE_INDEX,
+        )
+        loss = ce_weight * ce.sum() + ent_weight * ent.sum()
+        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight)
+        ce = ce.view(batch_shape)
+        ent = ent.view(batch_shape)
+        ctx.mark_non_differentiable(ce, ent)
+        return loss, ce, ent
+
+    @staticmethod
+    def backward(ctx, dloss, _g_ce, _g_ent):
+        d_hidden, d_weight = ctx.saved_tensors
+        d_hidden, d_weight = gk._scale_grads(d_hidden, d_weight, dloss)
+        return d_hidden, d_weight, None, None, None, None, None, None, None
+
+
+def vocab_parallel_megakernel(
+    hidden_states: Tensor,
+    weight_shard: Tensor,
+    target: Tensor,
+    vocab_start: int,
+    vocab_size: int,
+    group=None,
+    chunk_size: int = 4096,
+    ce_weight: float = 1.0,
+    ent_weight: float = -1.0,
+) -> Tuple[Tensor, Tensor, Tensor]:
+    """Vocabulary-parallel gemm_megakernel_fast. Returns (loss, ce_loss, entropy), identical on
+    every rank; loss.backward() gives every rank the full d_hidden and its own weight-slice
+    gradient."""
+    return VocabParallelMegakernel.apply(hidden_states, weight_shard, target, vocab_start, vocab_size, group,
+                                         chunk_size, ce_weight, ent_weight)

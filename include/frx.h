@@ -1,0 +1,139 @@
+/*
+ * frx.h -- C ABI of libfrx.so, the B200 (sm_100a) engine behind the drop-in
+ * fast_reduction.gemm_kernel API: fused linear + cross-entropy + entropy.
+ *
+ * Conventions (all entry points):
+ *   - Every pointer is a device pointer owned by the caller; the library allocates no device
+ *     memory. Matrices are row-major with an explicit leading dimension in elements.
+ *   - Every call is asynchronous on `stream` (a cudaStream_t, passed as void*; NULL = legacy
+ *     default stream) and returns FRX_OK (0) or an FRX_ERR_* code. The message for the last
+ *     failure on the calling thread is available from frx_last_error(). Nothing aborts.
+ *   - `status` (optional, may be NULL) is a device int the kernels OR FRX_STATUS_* bits into
+ *     when they detect a problem while running (a pipeline wait that timed out, a target id
+ *     outside the vocabulary). The host reads it whenever it chooses to synchronise.
+ *   - Vocabulary sharding: a call may cover only the slice [vocab_offset, vocab_offset +
+ *     vocab_shard) of the vocabulary; `target` always holds global vocabulary ids.
+ *   - bf16 operands need 16-byte aligned bases and leading dimensions that are multiples of 8.
+ *
+ * The forward partials contract: for vocabulary tile t (columns [256 t, 256 t + 256) of the
+ * shard) and row r, partials[t * tile_stride + r] holds four floats
+ *     m  = max_j z_j,  s = sum_j exp(z_j - m),  u = sum_j (z_j - m) exp(z_j - m),  zt
+ * where zt = z_target when the row's target falls in the tile, else 0. The reference's own
+ * epilogue stores sx = sum_j z_j exp(z_j - m) in the third slot instead of u; frx_finalize
+ * accepts that layout with FRX_PARTIALS_REF_LAYOUT.
+ */
+#ifndef FRX_H_
+#define FRX_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FRX_API __attribute__((visibility("default")))
+#else
+#define FRX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FRX_ABI_VERSION 1
+
+#define FRX_OK 0
+#define FRX_ERR_INVALID_ARG 1
+#define FRX_ERR_UNSUPPORTED 2
+#define FRX_ERR_CUDA 3
+
+#define FRX_DTYPE_BF16 0
+#define FRX_DTYPE_F32 1
+
+/* Width of one vocabulary tile of the forward partials (columns per partial). */
+#define FRX_VOCAB_TILE 256
+
+/* frx_finalize flags */
+#define FRX_PARTIALS_REF_LAYOUT 1 /* third slot holds sum z*exp(z-m) (reference layout) */
+
+/* device status bits */
+#define FRX_STATUS_TIMEOUT_PRODUCER 1
+#define FRX_STATUS_TIMEOUT_MMA 2
+#define FRX_STATUS_TIMEOUT_EPILOGUE 4
+#define FRX_STATUS_BAD_TARGET 8
+#define FRX_STATUS_DRAIN_TIMEOUT 16
+
+/* ABI version of the loaded library (FRX_ABI_VERSION it was built with). */
+FRX_API int frx_abi_version(void);
+
+/* Message describing the most recent failed call on this thread ("" if none). */
+FRX_API const char* frx_last_error(void);
+
+/*
+ * Forward GEMM with the CE / entropy reduction fused into its epilogue.
+ * Replaces the reference's GEMM-epilogue launch `_gemm_ce_entropy_kernel`
+ * (fast_reduction/gemm_kernel.py:58-165; epilogue math gemm_ce_entropy_epilogue.py:184-271)
+ * and, with `logits` non-NULL, the logits-writing variant `_gemm_ce_entropy_bwd_kernel`
+ * (gemm_kernel.py:168-273, gemm_ce_entropy_bwd_epilogue.py:218).
+ *
+ *   z[r, j]  = sum_k hidden[r, k] * weight[j, k]        (bf16 x bf16 -> fp32, TMEM)
+ *   hidden   [rows, hidden_dim] bf16, row stride ld_hidden
+ *   weight   [vocab_shard, hidden_dim] bf16, row stride ld_weight (the shard's rows)
+ *   target   [rows] int64 global ids, or NULL (then zt = 0)
+ *   partials [ceil(vocab_shard / 256) * tile_stride] x float4, tile_stride >= rows
+ *   logits   optional fp32 [rows, ld_logits] output of every z (NULL: logits never leave the chip)
+ */
+FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
+                     const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
+                     int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
+                     int64_t ld_logits, int* status, void* stream);
+
+/*
+ * Merges per-tile partials into per-row results.
+ * Replaces the reference's `Finalize` kernel and its custom ops
+ * (fast_reduction/gemm_ce_entropy_finalize.py:29-102, 123-212).
+ *
+ *   lse = M + log S,  entropy = log S - U / S,  ce = lse - ZT,  log_probs = -ce
+ * Rows whose target equals ignore_index get ce = 0 and log_probs = 0 (torch nll_loss
+ * semantics); targets outside [0, vocab_size) give NaN and set FRX_STATUS_BAD_TARGET.
+ * target may be NULL (no CE semantics check). Any of ce/entropy/lse/log_probs may be NULL.
+ * `merged` (optional, float4 per row) receives the merged (M, S, U, ZT) in the u layout, for a
+ * further cross-shard merge (call frx_finalize again with n_tiles = number of shards).
+ */
+FRX_API int frx_finalize(const float* partials, int64_t n_tiles, int64_t rows, int64_t tile_stride, int flags,
+                 const int64_t* target, int64_t vocab_size, int64_t ignore_index, float* ce,
+                 float* entropy, float* lse, float* log_probs, float* merged, int* status, void* stream);
+
+/*
+ * dlogits of loss = sum_r g_ce[r] * ce[r] + g_ent[r] * entropy[r] for one vocabulary shard:
+ *   p = exp(z - lse);  dz = p * (g_ce - g_ent * (log p + H)) - g_ce * [j == target]
+ * Replaces `ComputeDlogits` / `compute_dlogits` (fast_reduction/cute_dlogits.py:32-100, 162-183).
+ * g_ce / g_ent: per-row fp32 vectors, or NULL to use the scalars ce_weight / ent_weight.
+ * Rows with target == ignore_index drop the CE term. out_dtype: FRX_DTYPE_BF16 or _F32.
+ */
+FRX_API int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t* target, const float* lse,
+                const float* entropy, const float* g_ce, const float* g_ent, float ce_weight,
+                float ent_weight, void* dlogits, int64_t ld_dlogits, int out_dtype, int64_t rows,
+                int64_t vocab_shard, int64_t vocab_offset, int64_t ignore_index, void* stream);
+
+/*
+ * d_hidden[rows, hidden_dim] = dlogits[rows, vocab_shard] @ weight[vocab_shard, hidden_dim]
+ * (bf16 in, fp32 accumulation, out_dtype out). Replaces the cuBLAS `torch.mm(dlogits, weight)`
+ * of the reference's megakernel (fast_reduction/gemm_kernel.py:859-862).
+ */
+FRX_API int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void* weight, int64_t ld_weight,
+                     void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows, int64_t hidden_dim,
+                     int64_t vocab_shard, int* status, void* stream);
+
+/*
+ * d_weight[vocab_shard, hidden_dim] = dlogits[rows, vocab_shard]^T @ hidden[rows, hidden_dim]
+ * accumulated over all `rows` in fp32 tensor memory and written once in out_dtype. Replaces
+ * the per-chunk `d_weight.add_(torch.mm(dlogits.t(), h_chunk).float())` and the final cast
+ * of the reference (fast_reduction/gemm_kernel.py:864-871).
+ */
+FRX_API int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
+                     void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
+                     int64_t hidden_dim, int64_t rows, int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRX_H_ */

@@ -1,0 +1,85 @@
+"""CPU: libfrx.so loads, exports exactly what include/frx.h declares, and rejects bad arguments
+with a status code and message (no abort, no GPU needed for argument checks)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parents[1]
+HEADER = REPO / "include" / "frx.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*FRX_API\s+(?:const\s+)?\w+\s*\*?\s*(frx_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    for must in ("frx_fwd_partials", "frx_finalize", "frx_dlogits", "frx_gemm_dhidden", "frx_gemm_dweight",
+                 "frx_last_error", "frx_abi_version"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from fast_reduction import _native as nat
+
+    lib = nat.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in frx.h but not exported"
+        assert name in nat.SIGNATURES, f"{name} has no ctypes signature in _native.py"
+
+
+def test_abi_version_and_error_string():
+    from fast_reduction import _native as nat
+
+    lib = nat.load()
+    hdr = HEADER.read_text()
+    ver = int(re.search(r"#define FRX_ABI_VERSION (\d+)", hdr).group(1))
+    assert lib.frx_abi_version() == ver
+    assert isinstance(lib.frx_last_error(), bytes)
+
+
+def test_constants_match_header():
+    from fast_reduction import _native as nat
+
+    hdr = HEADER.read_text()
+    for name in ("FRX_OK", "FRX_ERR_INVALID_ARG", "FRX_ERR_UNSUPPORTED", "FRX_ERR_CUDA", "FRX_DTYPE_BF16",
+                 "FRX_DTYPE_F32", "FRX_VOCAB_TILE", "FRX_PARTIALS_REF_LAYOUT", "FRX_STATUS_BAD_TARGET",
+                 "FRX_STATUS_TIMEOUT_PRODUCER", "FRX_STATUS_TIMEOUT_MMA", "FRX_STATUS_TIMEOUT_EPILOGUE",
+                 "FRX_STATUS_DRAIN_TIMEOUT"):
+        val = int(re.search(rf"#define {name} (\d+)", hdr).group(1))
+        assert getattr(nat, name) == val, name
+
+
+def test_invalid_arguments_return_codes_without_gpu():
+    from fast_reduction import _native as nat
+
+    lib = nat.load()
+    # negative sizes are rejected before any CUDA call
+    rc = lib.frx_fwd_partials(None, 0, None, 0, None, -1, 10, 64, 0, None, 0, None, 0, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG
+    assert b"bad sizes" in lib.frx_last_error()
+    rc = lib.frx_fwd_partials(1 << 20, 64, 1 << 21, 64, None, 8, 10, 60, 0, 1 << 22, 8, None, 0, None, None)
+    assert rc == nat.FRX_ERR_UNSUPPORTED  # hidden_dim not a multiple of 8
+    rc = lib.frx_finalize(None, 3, 10, 5, 0, None, 0, 0, None, None, None, None, None, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # tile_stride < rows
+    rc = lib.frx_finalize(None, 1, 10, 10, 0x40, None, 0, 0, None, None, None, None, None, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # unknown flag
+    rc = lib.frx_dlogits(None, 0, None, None, None, None, None, 1.0, -1.0, None, 0, 7, 4, 4, 0, 0, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG
+    rc = lib.frx_gemm_dhidden(None, 0, None, 0, None, 0, 0, -5, 64, 64, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG
+    rc = lib.frx_gemm_dweight(None, 0, None, 0, None, 0, 0, 64, 64, 0, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG
+
+
+def test_empty_problems_are_noops():
+    from fast_reduction import _native as nat
+
+    lib = nat.load()
+    assert lib.frx_fwd_partials(None, 0, None, 0, None, 0, 10, 64, 0, None, 0, None, 0, None, None) == nat.FRX_OK
+    assert lib.frx_finalize(None, 0, 0, 0, 0, None, 0, 0, None, None, None, None, None, None, None) == nat.FRX_OK

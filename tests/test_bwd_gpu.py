@@ -1,0 +1,193 @@
+"""GPU parity tests of the training path: dlogits kernel, the two backward tcgen05 GEMMs, and the
+gemm_megakernel_fast autograd op (reference tests/test_backward.py:474-603 plus stricter gates)."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import reference_math as rm
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    from fast_reduction import _native as nat
+
+    yield
+    torch.cuda.synchronize()
+    nat.raise_on_status(torch.device(DEV))
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_dlogits_kernel_matches_oracle(out_dtype):
+    from fast_reduction import ops
+
+    M, V, off = 70, 1003, 500
+    g = torch.Generator().manual_seed(4)
+    z = torch.randn(M, V, generator=g) * 3
+    t = torch.randint(off, off + V, (M,), generator=g)
+    t[::9] = -100
+    t[1::13] = off + V + 3  # target on another shard
+    lse = torch.logsumexp(z.double(), -1)
+    p = torch.softmax(z.double(), -1)
+    ent = -(p * torch.log_softmax(z.double(), -1)).sum(-1)
+    gce = torch.rand(M, generator=g)
+    gent = torch.randn(M, generator=g)
+    ld = 1008
+    zd = torch.zeros(M, ld, device=DEV)
+    zd[:, :V] = z.to(DEV)
+    out = torch.zeros(M, ld, device=DEV, dtype=out_dtype)
+    ops.dlogits(zd, t.to(DEV), lse.float().to(DEV), ent.float().to(DEV), out, rows=M, vocab_shard=V,
+                g_ce=gce.to(DEV), g_ent=gent.to(DEV), vocab_offset=off, ignore_index=-100)
+    exp = rm.dlogits(z.double().numpy(), t.numpy(), lse.numpy(), ent.numpy(), gce.numpy(), gent.numpy(),
+                     vocab_offset=off)
+    got = out[:, :V].float().cpu().numpy()
+    if out_dtype == torch.float32:
+        np.testing.assert_allclose(got, exp, atol=2e-6, rtol=1e-4)
+    else:
+        np.testing.assert_allclose(got, exp, atol=1e-5, rtol=8e-3)
+    assert (out[:, V:] == 0).all()  # padding untouched
+    # scalar weights path
+    out2 = torch.zeros(M, ld, device=DEV, dtype=out_dtype)
+    ops.dlogits(zd, t.to(DEV), lse.float().to(DEV), ent.float().to(DEV), out2, rows=M, vocab_shard=V,
+                ce_weight=0.5, ent_weight=-2.0, vocab_offset=off, ignore_index=-100)
+    exp2 = rm.dlogits(z.double().numpy(), t.numpy(), lse.numpy(), ent.numpy(), 0.5, -2.0, vocab_offset=off)
+    tol = dict(atol=2e-6, rtol=1e-4) if out_dtype == torch.float32 else dict(atol=1e-5, rtol=8e-3)
+    np.testing.assert_allclose(out2[:, :V].float().cpu().numpy(), exp2, **tol)
+
+
+def test_compute_dlogits_mirror_no_ignore_rule():
+    """The reference's compute_dlogits has no ignore rule (cute_dlogits.py:98): a -100 target keeps
+    the p * g_ce term and matches no column."""
+    from fast_reduction.cute_dlogits import compute_dlogits
+
+    M, V = 32, 300
+    z = torch.randn(M, V, device=DEV) * 2
+    t = torch.randint(0, V, (M,), device=DEV, dtype=torch.int32)
+    t[0] = -100
+    lse = torch.logsumexp(z, -1)
+    ent = -(torch.softmax(z, -1) * torch.log_softmax(z, -1)).sum(-1)
+    gce = torch.ones(M, device=DEV)
+    gent = -torch.ones(M, device=DEV)
+    dz = compute_dlogits(z, t, lse, ent, gce, gent)
+    exp = rm.dlogits(z.double().cpu().numpy(), t.cpu().numpy(), lse.cpu().numpy(), ent.cpu().numpy(), 1.0, -1.0,
+                     ignore_index=None)
+    np.testing.assert_allclose(dz.cpu().numpy(), exp, atol=3e-6, rtol=1e-4)
+
+
+@pytest.mark.parametrize("rows,V,H", [(300, 1000, 200), (256, 512, 256), (129, 77, 64), (1000, 4096, 1024)])
+def test_backward_gemms_match_fp32(rows, V, H):
+    from fast_reduction import ops
+
+    g = torch.Generator(device=DEV).manual_seed(rows + V)
+    ldz = ops.round_up(V, 8)
+    dz = torch.zeros(rows, ldz, device=DEV, dtype=torch.bfloat16)
+    dz[:, :V] = (torch.randn(rows, V, device=DEV, generator=g) * 0.1).to(torch.bfloat16)
+    w = torch.randn(V, H, device=DEV, generator=g).to(torch.bfloat16)
+    h = torch.randn(rows, H, device=DEV, generator=g).to(torch.bfloat16)
+    dh = torch.empty(rows, H, device=DEV, dtype=torch.float32)
+    dw = torch.empty(V, H, device=DEV, dtype=torch.float32)
+    ops.gemm_dhidden(dz, w, dh, rows=rows, vocab_shard=V)
+    ops.gemm_dweight(dz, h, dw, rows=rows, vocab_shard=V)
+    dz64 = dz[:, :V].double()
+    exp_dh = dz64 @ w.double()
+    exp_dw = dz64.T @ h.double()
+    torch.testing.assert_close(dh.double(), exp_dh, atol=1e-4 * max(1.0, V / 1000), rtol=1e-4)
+    torch.testing.assert_close(dw.double(), exp_dw, atol=1e-4 * max(1.0, rows / 1000), rtol=1e-4)
+    dh16 = torch.empty(rows, H, device=DEV, dtype=torch.bfloat16)
+    ops.gemm_dhidden(dz, w, dh16, rows=rows, vocab_shard=V)
+    torch.testing.assert_close(dh16.float(), dh.to(torch.bfloat16).float(), atol=0, rtol=0)
+
+
+def test_megakernel_matches_reference_test():
+    """Reference tests/test_backward.py:474-497 (B=256, H=128, V=1024, N(0,1) weights): grad MAE < 0.05."""
+    from fast_reduction.gemm_kernel import gemm_megakernel_fast
+
+    torch.manual_seed(123)
+    B, H, V = 256, 128, 1024
+    hidden = torch.randn(B, H, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    weight = torch.randn(V, H, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    target = torch.randint(0, V, (B,), device=DEV)
+    loss, ce, ent = gemm_megakernel_fast(hidden, weight, target, chunk_size=B)
+    loss.backward()
+    _, _, dh_ref, dw_ref = rm.fp32_reference_grads(hidden.detach().cpu(), weight.detach().cpu(), target.cpu())
+    assert (hidden.grad.float().cpu() - dh_ref).abs().mean() < 0.05
+    assert (weight.grad.float().cpu() - dw_ref).abs().mean() < 0.05
+    ce_ref, ent_ref, _, _ = rm.fp32_reference(hidden.detach().cpu(), weight.detach().cpu(), target.cpu())
+    torch.testing.assert_close(ce.cpu(), ce_ref, atol=1e-2, rtol=1e-2)
+    torch.testing.assert_close(loss.detach().cpu(), ce_ref.sum() - ent_ref.sum(), atol=2.0, rtol=1e-3)
+
+
+def test_megakernel_config0_gates():
+    """configs[0]-shaped training pass (B=1024, H=1024, V=32000, chunk 512; ce_weight 1, ent_weight -1):
+    loss, d_hidden and d_weight against fp32 autograd (north-star MAE gate 2e-3 on dH / dW)."""
+    from fast_reduction.gemm_kernel import gemm_megakernel_fast
+
+    h, w, t = rm.make_inputs(1024, 1024, 32000, seed=0)
+    hd = h.to(DEV).requires_grad_(True)
+    wd = w.to(DEV).requires_grad_(True)
+    loss, ce, ent = gemm_megakernel_fast(hd, wd, t.to(DEV), chunk_size=512)
+    loss.backward()
+    ce_ref, ent_ref, dh_ref, dw_ref = rm.fp32_reference_grads(h.to(DEV), w.to(DEV), t.to(DEV))
+    assert (ce - ce_ref).abs().mean() <= 2e-3
+    assert (ent - ent_ref).abs().mean() <= 1e-4
+    assert (hd.grad.float() - dh_ref).abs().mean() <= 2e-3
+    assert (wd.grad.float() - dw_ref).abs().mean() <= 2e-3
+    # relative gates: the gradients themselves are small at this scale
+    rel_dh = (hd.grad.float() - dh_ref).norm() / dh_ref.norm()
+    rel_dw = (wd.grad.float() - dw_ref).norm() / dw_ref.norm()
+    assert rel_dh < 1e-2 and rel_dw < 1e-2, (rel_dh, rel_dw)
+
+
+def test_megakernel_non_aligned_vocab_and_ignore_index():
+    """Reference tests/test_backward.py:531-553 (V=1000) plus ignore_index rows."""
+    from fast_reduction.gemm_kernel import gemm_megakernel_fast
+
+    h, w, t = rm.make_inputs(256, 64, 1000, seed=777, weight_std=0.3, ignore_frac=0.05)
+    hd = h.to(DEV).requires_grad_(True)
+    wd = w.to(DEV).requires_grad_(True)
+    loss, ce, ent = gemm_megakernel_fast(hd, wd, t.to(DEV), chunk_size=256)
+    loss.backward()
+    assert not torch.isnan(hd.grad).any() and not torch.isnan(wd.grad).any()
+    ce_ref, ent_ref, dh_ref, dw_ref = rm.fp32_reference_grads(h, w, t)
+    assert (hd.grad.float().cpu() - dh_ref).abs().mean() < 2e-3
+    assert (wd.grad.float().cpu() - dw_ref).abs().mean() < 2e-3
+    assert (ce.cpu()[t == -100] == 0).all()
+
+
+def test_megakernel_detached_outputs_and_shapes():
+    from fast_reduction.gemm_kernel import gemm_megakernel_fast
+
+    torch.manual_seed(42)
+    B, H, V = 128, 64, 512
+    hidden = torch.randn(2, B // 2, H, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    weight = torch.randn(V, H, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    target = torch.randint(0, V, (2, B // 2), device=DEV)
+    loss, ce, ent = gemm_megakernel_fast(hidden, weight, target, chunk_size=B)
+    assert loss.requires_grad and not ce.requires_grad and not ent.requires_grad
+    assert loss.dim() == 0 and ce.shape == (2, B // 2) and ent.shape == (2, B // 2)
+    loss.backward()
+    assert hidden.grad.shape == hidden.shape and hidden.grad.dtype == torch.bfloat16
+    assert weight.grad.shape == weight.shape and weight.grad.dtype == torch.bfloat16
+
+
+def test_megakernel_chunked_equals_unchunked_and_dloss_scaling():
+    """Reference tests/test_backward.py:576-603: chunked and unchunked gradients agree; here both are
+    bit-identical (d_weight is accumulated over all rows in one GEMM either way)."""
+    from fast_reduction.gemm_kernel import gemm_megakernel_fast
+
+    h, w, t = rm.make_inputs(256, 128, 1024, seed=42, weight_std=0.2)
+    grads = []
+    for chunk, scale in ((256, 1.0), (64, 1.0), (100, 3.0)):
+        hd = h.to(DEV).requires_grad_(True)
+        wd = w.to(DEV).requires_grad_(True)
+        loss, _, _ = gemm_megakernel_fast(hd, wd, t.to(DEV), chunk_size=chunk)
+        (loss * scale).backward()
+        grads.append((hd.grad, wd.grad))
+    assert torch.equal(grads[0][0], grads[1][0])
+    assert torch.equal(grads[0][1], grads[1][1])
+    torch.testing.assert_close(grads[2][0].float(), 3.0 * grads[0][0].float(), atol=1e-6, rtol=1e-2)
+    torch.testing.assert_close(grads[2][1].float(), 3.0 * grads[0][1].float(), atol=1e-6, rtol=1e-2)

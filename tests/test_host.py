@@ -1,0 +1,79 @@
+"""CPU: host-side validation of the drop-in API raises before any device work, mirroring the
+reference's Python-level error behaviour (asserts / KeyError / NotImplementedError)."""
+
+import pytest
+import torch
+
+from fast_reduction import gemm_kernel as gk
+from fast_reduction import ops
+from fast_reduction.gemm_ce_entropy_finalize import finalize_ce_entropy
+from fast_reduction.cute_dlogits import compute_dlogits
+
+
+def _inputs(dtype=torch.bfloat16, B=8, H=16, V=40):
+    return torch.randn(B, H).to(dtype), torch.randn(V, H).to(dtype), torch.randint(0, V, (B,))
+
+
+def test_cpu_tensors_rejected_no_fallback():
+    h, w, t = _inputs()
+    with pytest.raises(ValueError, match="CUDA"):
+        gk.gemm_fused_ce_entropy(h, w, t)
+    with pytest.raises(ValueError, match="CUDA"):
+        gk.gemm_megakernel_fast(h, w, t)
+
+
+def test_bias_not_supported():
+    h, w, t = _inputs()
+    with pytest.raises(NotImplementedError):
+        gk.gemm_fused_ce_entropy(h, w, t, bias=torch.zeros(40))
+
+
+def test_non_bf16_rejected():
+    h, w, t = _inputs(dtype=torch.float32)
+    with pytest.raises(NotImplementedError, match="bf16"):
+        gk.gemm_fused_ce_entropy(h, w, t)
+
+
+def test_shape_checks():
+    h, w, t = _inputs()
+    with pytest.raises(ValueError, match="hidden size mismatch"):
+        gk.gemm_fused_ce_entropy(h, w[:, :8], t)
+    with pytest.raises(ValueError, match="target has"):
+        gk.gemm_fused_ce_entropy(h, w, t[:3])
+    h2 = torch.randn(8, 12).to(torch.bfloat16)
+    with pytest.raises(NotImplementedError, match="multiple of 8"):
+        gk.gemm_fused_ce_entropy(h2, torch.randn(40, 12).to(torch.bfloat16), t)
+    with pytest.raises(TypeError):
+        gk.gemm_fused_ce_entropy(h, w, t.float())
+
+
+def test_finalize_mirror_checks():
+    with pytest.raises(ValueError, match=r"\[N_tiles, M, 4\]"):
+        finalize_ce_entropy(torch.zeros(2, 3, 5), 2)
+    with pytest.raises(ValueError, match="n_tiles"):
+        finalize_ce_entropy(torch.zeros(2, 3, 4), 3)
+
+
+def test_dlogits_mirror_checks():
+    from fast_reduction import cute_dlogits
+
+    with pytest.raises(ValueError, match="CUDA"):
+        compute_dlogits(torch.zeros(2, 3), torch.zeros(2, dtype=torch.int64), torch.zeros(2), torch.zeros(2),
+                        torch.zeros(2), torch.zeros(2))
+    with pytest.raises(KeyError):  # the reference maps only int32 / int64 targets
+        cute_dlogits._prep_target(torch.zeros(2, dtype=torch.int16))
+
+
+def test_tile_helpers():
+    assert ops.n_vocab_tiles(128256) == 501
+    assert ops.n_vocab_tiles(256) == 1 and ops.n_vocab_tiles(257) == 2
+    assert ops.round_up(1000, 8) == 1000 and ops.round_up(1001, 8) == 1008
+
+
+def test_lazy_exports():
+    import fast_reduction
+
+    assert fast_reduction.gemm_fused_ce_entropy is gk.gemm_fused_ce_entropy
+    assert fast_reduction.gemm_megakernel_fast is gk.gemm_megakernel_fast
+    with pytest.raises(AttributeError):
+        fast_reduction.does_not_exist
