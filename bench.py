@@ -224,7 +224,7 @@ def cpu_baseline(B, H, V, chunk, budget_s: float = 12.0) -> dict:
     t0 = time.perf_counter()
     rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
     probe = time.perf_counter() - t0
-    rows = int(max(64, min(4096, rows * budget_s / max(probe, 1e-3)))) // 64 * 64
+    rows = int(max(64, min(B, rows * budget_s / max(probe, 1e-3)))) // 64 * 64
     h = torch.randn(rows, H, generator=g).to(torch.bfloat16)
     t = torch.randint(0, V, (rows,), generator=g)
     t0 = time.perf_counter()
