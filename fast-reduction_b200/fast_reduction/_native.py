@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "frx_gemm_dhidden": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
     "frx_gemm_dweight": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
+    "frx_fwd_ce_entropy_noalloc": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
 }
 
 _lib = None

@@ -132,6 +132,23 @@ FRX_API int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void
                      void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
                      int64_t hidden_dim, int64_t rows, int* status, void* stream);
 
+/*
+ * Forward CE / entropy / lse / log_probs in one call that allocates no device memory: the
+ * partials live in a 32 MiB scratch array that is part of the library image on each GPU.
+ * No counterpart in the reference. For callers that cannot call cudaMalloc (a framework that
+ * owns all device memory, a serving loop that must not synchronise on an allocation, a fixed
+ * memory budget). Limit: ceil(vocab_size / 256) * rows * 16 bytes <= 32 MiB (e.g. at most
+ * 4096 rows per call at V = 128256); larger calls return FRX_ERR_INVALID_ARG. All calls on a
+ * device share the scratch, so calls that overlap on the GPU race; the first call on a device
+ * looks up the scratch address and should come before any stream capture. The whole
+ * vocabulary is one shard (targets are plain vocabulary ids).
+ */
+FRX_API int frx_fwd_ce_entropy_noalloc(const void* hidden, int64_t ld_hidden, const void* weight,
+                                       int64_t ld_weight, const int64_t* target, int64_t rows,
+                                       int64_t vocab_size, int64_t hidden_dim, int64_t ignore_index,
+                                       float* ce, float* entropy, float* lse, float* log_probs, int* status,
+                                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif
