@@ -37,6 +37,14 @@ void set_error(const char* fmt, ...) {
   va_end(ap);
 }
 
+bool use_pair_kernel() {
+  static const bool pair = [] {
+    const char* v = getenv("FRX_GEMM_VARIANT");
+    return !(v != nullptr && strcmp(v, "single") == 0);
+  }();
+  return pair;
+}
+
 int sm_count(int* out) {
   int dev = 0;
   FRX_CUDA_CHECK(cudaGetDevice(&dev));
@@ -54,24 +62,33 @@ int sm_count(int* out) {
   return FRX_OK;
 }
 
-int encode_bf16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
-                   int box_cols) {
+static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, int64_t rows,
+                     int64_t cols, int64_t ld, int box_rows, int box_cols) {
   EncodeTiledFn fn = get_encode_fn();
   FRX_REQUIRE(fn != nullptr, FRX_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the CUDA driver");
-  FRX_REQUIRE(aligned16(base), FRX_ERR_INVALID_ARG, "bf16 operand base %p is not 16-byte aligned", base);
-  FRX_REQUIRE(ld % 8 == 0, FRX_ERR_INVALID_ARG, "bf16 operand leading dimension %lld is not a multiple of 8",
-              (long long)ld);
+  FRX_REQUIRE(aligned16(base), FRX_ERR_INVALID_ARG, "matrix base %p is not 16-byte aligned", base);
+  FRX_REQUIRE((ld * elem_bytes) % 16 == 0, FRX_ERR_INVALID_ARG,
+              "matrix leading dimension %lld x %d bytes is not a multiple of 16", (long long)ld, elem_bytes);
   FRX_REQUIRE(rows >= 1 && cols >= 1 && ld >= cols, FRX_ERR_INVALID_ARG,
-              "bad operand extents rows=%lld cols=%lld ld=%lld", (long long)rows, (long long)cols, (long long)ld);
+              "bad matrix extents rows=%lld cols=%lld ld=%lld", (long long)rows, (long long)cols, (long long)ld);
   cuuint64_t gdim[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld) * 2u};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(ld) * static_cast<cuuint64_t>(elem_bytes)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estride[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gdim, gstride, box, estride,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   FRX_REQUIRE(r == CUDA_SUCCESS, FRX_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
   return FRX_OK;
+}
+
+int encode_bf16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                   int box_cols) {
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, box_rows, box_cols);
+}
+
+int encode_f32_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                  int box_cols) {
+  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, rows, cols, ld, box_rows, box_cols);
 }
 
 }  // namespace frx

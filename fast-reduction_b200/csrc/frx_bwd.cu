@@ -13,6 +13,9 @@ namespace frx {
 // Writes the fp32 accumulator tile as bf16 or fp32 rows: each thread owns one output row and
 // stores 32 consecutive columns per TMEM load.
 struct StoreEpilogue {
+  static constexpr int kSmemPerWarp = 0;
+  static constexpr int kSmemBytes = 0;
+
   struct Params {
     void* out;
     int64_t ld_out;
@@ -23,8 +26,8 @@ struct StoreEpilogue {
   };
 
   template <class Release>
-  __device__ __forceinline__ static void run(const Params& p, uint32_t tacc, int m_blk, int n_blk, int q, int lane,
-                                             Release release) {
+  __device__ __forceinline__ static void run(const Params& p, uint8_t* /*stage*/, uint32_t tacc, int m_blk, int n_blk,
+                                             int q, int lane, Release release) {
     const int row = m_blk * kBM + q * 32 + lane;
     const int n0 = n_blk * kBN;
     const int ncols = min(kBN, p.cols - n0);
@@ -74,6 +77,8 @@ struct StoreEpilogue {
     }
     release();
   }
+
+  __device__ __forceinline__ static void finish(const Params&, int) {}
 };
 
 static int check_out(void* out, int64_t ld, int64_t cols, int out_dtype, const char* who) {

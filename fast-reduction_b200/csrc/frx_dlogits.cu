@@ -4,21 +4,27 @@
 //   dz_j = p_j * (g_ce - g_ent * (log p_j + H)) - g_ce * [j == target]
 //
 // (reference: fast_reduction/cute_dlogits.py:87-100). Pure streaming kernel, HBM-bound:
-// reads fp32 logits once, writes bf16 (or fp32) dlogits once. Each thread handles 8
-// consecutive columns (two 16-byte loads, one 16-byte bf16 store); the per-row constants
-// A = g_ce - g_ent * H and B = -g_ent are formed once per thread.
+// reads fp32 logits once, writes bf16 (or fp32) dlogits once. Each thread handles 16
+// consecutive columns of a row (four 16-byte streaming loads issued back to back, two 16-byte
+// bf16 stores); the per-row constants A = g_ce - g_ent * H and B = -g_ent are formed once per
+// thread, after the loads are in flight.
 #include "frx_host.cuh"
 
 namespace frx {
 
 constexpr int kDlThreads = 256;
-constexpr int kDlVec = 8;
+constexpr int kDlVec = 16;  // columns per thread: four 16-byte loads in flight
 constexpr int kDlColsPerBlock = kDlThreads * kDlVec;
 
 __device__ __forceinline__ float dz_value(float z, float row_lse, float a, float b) {
   const float lp = z - row_lse;
   const float p = ex2_approx(lp * kLog2e);
   return p * fmaf(b, lp, a);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
 __global__ void __launch_bounds__(kDlThreads)
@@ -28,7 +34,24 @@ __global__ void __launch_bounds__(kDlThreads)
                    int64_t ld_out, int out_f32, int64_t rows, int64_t cols, int64_t vocab_offset,
                    int64_t ignore_index, int vec_ok) {
   const int64_t c0 = (static_cast<int64_t>(blockIdx.x) * kDlThreads + threadIdx.x) * kDlVec;
+  if (c0 >= cols) return;
+  const bool full = vec_ok && c0 + kDlVec <= cols;
   for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const float* zrow = logits + row * ld_logits;
+    float z[kDlVec];
+    if (full) {
+#pragma unroll
+      for (int i = 0; i < kDlVec; i += 4) {
+        const float4 q = __ldcs(reinterpret_cast<const float4*>(zrow + c0 + i));
+        z[i] = q.x;
+        z[i + 1] = q.y;
+        z[i + 2] = q.z;
+        z[i + 3] = q.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kDlVec; ++i) z[i] = (c0 + i < cols) ? zrow[c0 + i] : 0.0f;
+    }
     const float gc = g_ce != nullptr ? g_ce[row] : ce_weight;
     const float ge = g_ent != nullptr ? g_ent[row] : ent_weight;
     const float row_lse = lse[row];
@@ -37,36 +60,25 @@ __global__ void __launch_bounds__(kDlThreads)
     float gc_t = gc;
     if (target != nullptr) {
       const int64_t t = target[row];
-      if (t == ignore_index) gc_t = 0.0f;
+      if (t == ignore_index) gc_t = 0.0f;  // CE term dropped for ignored rows; entropy term kept
       tcol = t - vocab_offset;
     }
-    // CE term dropped for ignored rows; entropy term kept.
     const float a = gc_t - ge * h;
     const float b = -ge;
-    if (c0 >= cols) continue;
-    const float* zrow = logits + row * ld_logits;
-    float z[kDlVec];
-    const bool full = c0 + kDlVec <= cols;
-    if (full && vec_ok) {
-      const float4 z0 = __ldcs(reinterpret_cast<const float4*>(zrow + c0));
-      const float4 z1 = __ldcs(reinterpret_cast<const float4*>(zrow + c0 + 4));
-      z[0] = z0.x; z[1] = z0.y; z[2] = z0.z; z[3] = z0.w;
-      z[4] = z1.x; z[5] = z1.y; z[6] = z1.z; z[7] = z1.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < kDlVec; ++i) z[i] = (c0 + i < cols) ? zrow[c0 + i] : 0.0f;
-    }
     float d[kDlVec];
 #pragma unroll
-    for (int i = 0; i < kDlVec; ++i) {
-      d[i] = dz_value(z[i], row_lse, a, b);
-      if (c0 + i == tcol) d[i] -= gc_t;
+    for (int i = 0; i < kDlVec; ++i) d[i] = dz_value(z[i], row_lse, a, b);
+    if (tcol >= c0 && tcol < c0 + kDlVec) {
+#pragma unroll
+      for (int i = 0; i < kDlVec; ++i)
+        if (c0 + i == tcol) d[i] -= gc_t;
     }
     if (out_f32) {
       float* orow = static_cast<float*>(out) + row * ld_out;
-      if (full && vec_ok) {
-        __stcs(reinterpret_cast<float4*>(orow + c0), make_float4(d[0], d[1], d[2], d[3]));
-        __stcs(reinterpret_cast<float4*>(orow + c0 + 4), make_float4(d[4], d[5], d[6], d[7]));
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < kDlVec; i += 4)
+          __stcs(reinterpret_cast<float4*>(orow + c0 + i), make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]));
       } else {
 #pragma unroll
         for (int i = 0; i < kDlVec; ++i)
@@ -74,17 +86,16 @@ __global__ void __launch_bounds__(kDlThreads)
       }
     } else {
       __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(out) + row * ld_out;
-      if (full && vec_ok) {
-        uint4 pk;
-        __nv_bfloat162 h0 = __floats2bfloat162_rn(d[0], d[1]);
-        __nv_bfloat162 h1 = __floats2bfloat162_rn(d[2], d[3]);
-        __nv_bfloat162 h2 = __floats2bfloat162_rn(d[4], d[5]);
-        __nv_bfloat162 h3 = __floats2bfloat162_rn(d[6], d[7]);
-        pk.x = *reinterpret_cast<uint32_t*>(&h0);
-        pk.y = *reinterpret_cast<uint32_t*>(&h1);
-        pk.z = *reinterpret_cast<uint32_t*>(&h2);
-        pk.w = *reinterpret_cast<uint32_t*>(&h3);
-        *reinterpret_cast<uint4*>(orow + c0) = pk;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < kDlVec; i += 8) {
+          uint4 pk;
+          pk.x = pack_bf16x2(d[i], d[i + 1]);
+          pk.y = pack_bf16x2(d[i + 2], d[i + 3]);
+          pk.z = pack_bf16x2(d[i + 4], d[i + 5]);
+          pk.w = pack_bf16x2(d[i + 6], d[i + 7]);
+          __stcs(reinterpret_cast<uint4*>(orow + c0 + i), pk);
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < kDlVec; ++i)

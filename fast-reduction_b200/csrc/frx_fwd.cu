@@ -9,6 +9,8 @@
 // The reference computes the same four numbers per (row, 256-column tile) in
 // fast_reduction/gemm_ce_entropy_epilogue.py:184-271 (its third slot is sum z exp(z - m)).
 // Columns at or beyond the shard's vocabulary size are skipped, not sentinel-filled.
+#include <cstring>
+
 #include "frx_host.cuh"
 
 namespace frx {
@@ -29,22 +31,27 @@ __device__ __forceinline__ float select32(const float (&v)[32], int idx) {
 }
 
 struct CEPartialsEpilogue {
+  // Two 32 x 32 fp32 staging blocks per epilogue warp for the optional logits store.
+  static constexpr int kSmemPerWarp = 2 * 32 * 32 * 4;
+  static constexpr int kSmemBytes = 4 * kSmemPerWarp;
+
   struct Params {
+    CUtensorMap tm_logits;  // fp32 [rows, vocab_shard] logits, 32 x 32 boxes, 128B swizzle
     const int64_t* target;
     int64_t vocab_offset;
     int rows;
     int vocab_shard;
     float4* partials;
     int64_t tile_stride;
-    float* logits;
-    int64_t ld_logits;
+    int has_logits;
   };
 
   template <class Release>
-  __device__ __forceinline__ static void run(const Params& p, uint32_t tacc, int m_blk, int n_blk, int q,
-                                             int lane, Release release) {
+  __device__ __forceinline__ static void run(const Params& p, uint8_t* stage, uint32_t tacc, int m_blk, int n_blk,
+                                             int q, int lane, Release release) {
     // Row handled by this thread: TMEM lane (q * 32 + lane) of the tile.
-    const int row = m_blk * kBM + q * 32 + lane;
+    const int row0 = m_blk * kBM + q * 32;
+    const int row = row0 + lane;
     const int n0 = n_blk * kBN;
     const int ncols = min(kBN, p.vocab_shard - n0);
     const bool row_ok = row < p.rows;
@@ -53,8 +60,7 @@ struct CEPartialsEpilogue {
       const long long lt = static_cast<long long>(p.target[row]) - p.vocab_offset - n0;
       if (lt >= 0 && lt < ncols) tcol = static_cast<int>(lt);
     }
-    float* lrow = (p.logits != nullptr && row_ok) ? p.logits + static_cast<int64_t>(row) * p.ld_logits + n0 : nullptr;
-    const bool lvec = lrow != nullptr && ((reinterpret_cast<uintptr_t>(lrow) & 15u) == 0);
+    const uint32_t stage_base = smem_u32(stage);
 
     float v[32];
     float mx0 = -INFINITY, mx1 = -INFINITY, zt = 0.0f;
@@ -76,16 +82,23 @@ struct CEPartialsEpilogue {
           if (j < lim) mx0 = fmaxf(mx0, v[j]);
       }
       if ((tcol >> 5) == c) zt = select32(v, tcol & 31);
-      if (lrow != nullptr) {
-        float* dst = lrow + c * 32;
-        if (lim >= 32 && lvec) {
+      if (p.has_logits) {
+        // Stage this warp's 32 x 32 block in shared memory (row = lane, 16-byte chunks XOR-swizzled
+        // by row % 8, which is both bank-conflict free and the TMA 128B-swizzle layout) and write it
+        // with one TMA store; rows / columns outside the matrix are clipped by the TMA unit.
+        const int buf = c & 1;
+        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer has read it
+        __syncwarp();
+        const uint32_t rowb = stage_base + static_cast<uint32_t>(buf * 4096 + lane * 128);
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (j < lim) dst[j] = v[j];
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(rowb + static_cast<uint32_t>((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                       v[4 * j + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&p.tm_logits, stage + buf * 4096, n0 + c * 32, row0);
+          bulk_commit_group();
         }
       }
     }
@@ -96,7 +109,7 @@ struct CEPartialsEpilogue {
     for (int c = 0; c < kBN / 32; ++c) {
       const int lim = ncols - c * 32;
       if (lim <= 0) break;
-      __syncwarp();  // tcgen05.ld is warp-collective: reconverge after per-row branches
+      __syncwarp();
       tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
       if (lim >= 32) {
 #pragma unroll
@@ -121,6 +134,12 @@ struct CEPartialsEpilogue {
     }
     release();  // accumulator buffer may now be overwritten by the next tile's MMAs
     if (row_ok) p.partials[static_cast<int64_t>(n_blk) * p.tile_stride + row] = make_float4(mx, s0 + s1, u0 + u1, zt);
+  }
+
+  // Called once per epilogue warp after its last tile: outstanding logits stores must finish
+  // before the CTA (and its staging shared memory) goes away.
+  __device__ __forceinline__ static void finish(const Params& p, int lane) {
+    if (p.has_logits && lane == 0) bulk_wait_all();
   }
 };
 
@@ -147,15 +166,22 @@ extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const voi
               "frx_fwd_partials: partials must be 16-byte aligned");
   FRX_REQUIRE(logits == nullptr || ld_logits >= vocab_shard, FRX_ERR_INVALID_ARG,
               "frx_fwd_partials: ld_logits %lld < vocab_shard %lld", (long long)ld_logits, (long long)vocab_shard);
+  FRX_REQUIRE(logits == nullptr || (ld_logits % 4 == 0 && aligned16(logits)), FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials: logits must be 16-byte aligned with ld_logits a multiple of 4 (got %lld)",
+              (long long)ld_logits);
   CEPartialsEpilogue::Params ep;
+  memset(&ep, 0, sizeof(ep));
+  if (logits != nullptr) {
+    const int rc = encode_f32_2d(&ep.tm_logits, logits, rows, vocab_shard, ld_logits, 32, 32);
+    if (rc) return rc;
+    ep.has_logits = 1;
+  }
   ep.target = target;
   ep.vocab_offset = vocab_offset;
   ep.rows = static_cast<int>(rows);
   ep.vocab_shard = static_cast<int>(vocab_shard);
   ep.partials = reinterpret_cast<float4*>(partials);
   ep.tile_stride = tile_stride;
-  ep.logits = logits;
-  ep.ld_logits = ld_logits;
   Operand a{hidden, ld_hidden, rows, hidden_dim, false};
   Operand b{weight, ld_weight, vocab_shard, hidden_dim, false};
   // A band of up to 64 row blocks (8192 rows, 64 MiB of bf16 hidden at H=4096) stays in L2

@@ -36,6 +36,9 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kMNBoxBytes = 64 * kBK * 2;  // one 64 (MN) x 64 (K) bf16 box, 8 KiB
 constexpr int kGemmSmemBytes = kStages * kStageBytes + 1024 /*barriers*/ + 1024 /*alignment slack*/;
 
+// Dynamic shared memory of a GEMM kernel whose epilogue needs `epi_bytes` of staging space.
+constexpr int gemm_smem_bytes(int ring_bytes, int epi_bytes) { return ring_bytes + epi_bytes + 2048; }
+
 // Grouped rasterisation over (m-block, n-block) tiles: tiles are taken in bands of `group`
 // m-blocks; inside a band the m-block index runs fastest. Concurrently resident CTAs then
 // share both the band's A rows and a narrow slice of B in L2.
@@ -58,12 +61,14 @@ struct TileSched {
 template <bool kAMN, bool kBMN, class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                        TileSched sched, int num_k_blocks, typename Epi::Params ep, int* status) {
+                        TileSched sched, int num_k_blocks, const __grid_constant__ typename Epi::Params ep,
+                        int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
   uint8_t* s_b = smem + kStages * kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(s_b + kStages * kBBytes);
+  uint8_t* s_epi = s_b + kStages * kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_epi + Epi::kSmemBytes);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
@@ -211,11 +216,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int m_blk, n_blk;
       sched.get(t, m_blk, n_blk);
       const uint32_t tacc = tmem_base + static_cast<uint32_t>(buf * kBN) + (static_cast<uint32_t>(q * 32) << 16);
-      Epi::run(ep, tacc, m_blk, n_blk, q, lane, [&]() {
+      Epi::run(ep, s_epi + q * Epi::kSmemPerWarp, tacc, m_blk, n_blk, q, lane, [&]() {
         tc_fence_before();
         mbar_arrive(&acc_empty[buf]);
       });
     }
+    Epi::finish(ep, lane);
   }
 
   tc_fence_before();
@@ -223,6 +229,228 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace frx
+
+namespace frx {
+
+// ---------------------------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2): a cluster of two CTAs on neighbouring SMs computes a
+// 256 x 256 output tile with one M = 256 MMA stream issued by the even CTA. Each CTA stages only
+// its own 128 rows of A and its own 128-row half of B (32 KiB per k-block instead of 48 KiB), so
+// per-SM shared-memory and L2 traffic per FLOP drop by a third against the single-CTA kernel and
+// the ring can be 6 stages deep. Each CTA's TMEM holds the fp32 accumulator of its 128 rows x 256
+// columns, and each CTA runs the epilogue on its own rows. No TMA multicast is used: every CTA
+// loads its own operands; only MMA-completion commits are multicast to both CTAs.
+//
+// Barriers: the even CTA's full[s] counts the bytes of both CTAs' loads (the odd CTA's TMA
+// completes on it through its shared::cluster address); the MMA commit frees empty[s] in both
+// CTAs; acc_full[b] is signalled in both CTAs; the even CTA's acc_empty[b] collects one arrival
+// per epilogue warp of both CTAs.
+// ---------------------------------------------------------------------------------------------
+//
+// Each pipeline stage carries K = 128 (two 64-deep SW128 sub-tiles per operand), i.e. 8 MMAs per
+// tcgen05.commit: every commit costs the tensor pipe a drain bubble of roughly one MMA, which at
+// 4 MMAs per commit held the pipe to ~79% busy and at 8 lets it run at ~99%.
+constexpr int kPairBK = 128;
+constexpr int kPairStages = 3;
+constexpr int kPairSubBytes = 128 * 64 * 2;  // 128 rows x 64 K of bf16, 16 KiB
+constexpr int kPairABytes = 2 * kPairSubBytes;
+constexpr int kPairHalfBBytes = 2 * kPairSubBytes;
+constexpr int kPairStageBytes = kPairABytes + kPairHalfBBytes;
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 1024;
+
+template <bool kAMN, bool kBMN, class Epi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                             TileSched sched, int num_k_blocks, const __grid_constant__ typename Epi::Params ep,
+                        int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_a = smem;
+  uint8_t* s_b = smem + kPairStages * kPairABytes;
+  uint8_t* s_epi = s_b + kPairStages * kPairHalfBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(s_epi + Epi::kSmemBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* acc_full = empty + kPairStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* mma_done = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_cta_rank();
+  const bool leader = rank == 0;
+  const int pair_id = static_cast<int>(blockIdx.x >> 1);
+  const int num_pairs = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated in both
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int t = pair_id; t < sched.num_tiles && ok; t += num_pairs) {
+        int pm, n_blk;
+        sched.get(t, pm, n_blk);
+        const int m0 = pm * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int n0 = n_blk * kBN + static_cast<int>(rank) * (kBN / 2);
+        for (int kb = 0; kb < num_k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
+          uint8_t* da = s_a + stage * kPairABytes;
+          uint8_t* db = s_b + stage * kPairHalfBBytes;
+#pragma unroll
+          for (int h = 0; h < kPairBK / 64; ++h) {
+            const int kh = kb * kPairBK + 64 * h;
+            if (kAMN) {
+#pragma unroll
+              for (int g = 0; g < kBM / 64; ++g)
+                tma_load_2d_pair(da + h * kPairSubBytes + g * kMNBoxBytes, &tm_a, bar, m0 + 64 * g, kh);
+            } else {
+              tma_load_2d_pair(da + h * kPairSubBytes, &tm_a, bar, kh, m0);
+            }
+            if (kBMN) {
+#pragma unroll
+              for (int g = 0; g < (kBN / 2) / 64; ++g)
+                tma_load_2d_pair(db + h * kPairSubBytes + g * kMNBoxBytes, &tm_b, bar, n0 + 64 * g, kh);
+            } else {
+              tma_load_2d_pair(db + h * kPairSubBytes, &tm_b, bar, kh, n0);
+            }
+          }
+          ++issued;
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        if (leader) {
+          const long long first = issued > kPairStages ? issued - kPairStages : 0;
+          for (long long j = first; j < issued; ++j)
+            mbar_wait_drain(&full[j % kPairStages], static_cast<uint32_t>((j / kPairStages) & 1), status);
+        } else {
+          // The odd CTA's copies complete on the even CTA's barriers; give them time to land.
+          const uint64_t t0 = global_timer_ns();
+          while (global_timer_ns() - t0 < kDrainLimitNs / 10) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = make_idesc_bf16_f32(2 * kBM, kBN, kAMN, kBMN);
+      constexpr uint32_t a_lbo = kAMN ? kMNBoxBytes : 16;
+      constexpr uint32_t b_lbo = kBMN ? kMNBoxBytes : 16;
+      constexpr uint32_t a_kstep = kAMN ? 16 * 128 : 32;
+      constexpr uint32_t b_kstep = kBMN ? 16 * 128 : 32;
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = pair_id; t < sched.num_tiles && ok; t += num_pairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBN);
+        for (int kb = 0; kb < num_k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(s_a + stage * kPairABytes);
+          const uint32_t b_addr = smem_u32(s_b + stage * kPairHalfBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kPairBK / 16; ++kk) {
+            const uint32_t sub = static_cast<uint32_t>(kk >> 2) * kPairSubBytes;
+            const uint32_t k = static_cast<uint32_t>(kk & 3);
+            const uint64_t adesc = make_smem_desc_sw128(a_addr + sub + k * a_kstep, a_lbo, 1024);
+            const uint64_t bdesc = make_smem_desc_sw128(b_addr + sub + k * b_kstep, b_lbo, 1024);
+            umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair_mc(&empty[stage], 0x3);  // frees this slot in both CTAs
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit_pair_mc(&acc_full[buf], 0x3);
+      }
+      umma_commit_pair(mma_done);
+      mbar_wait_drain(mma_done, 0, status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue warps (both CTAs)
+    const int q = warp & 3;
+    int local = 0;
+    for (int t = pair_id; t < sched.num_tiles; t += num_pairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      int ok = 1;
+      if (lane == 0)
+        ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, status, kStatusTimeoutEpilogue) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      tc_fence_after();
+      int pm, n_blk;
+      sched.get(t, pm, n_blk);
+      const uint32_t tacc = tmem_base + static_cast<uint32_t>(buf * kBN) + (static_cast<uint32_t>(q * 32) << 16);
+      Epi::run(ep, s_epi + q * Epi::kSmemPerWarp, tacc, pm * 2 + static_cast<int>(rank), n_blk, q, lane, [&]() {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&acc_empty[buf]), 0));
+      });
+    }
+    Epi::finish(ep, lane);
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its peer may still touch its barriers or smem
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
 }
 

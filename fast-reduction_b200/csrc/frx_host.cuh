@@ -47,6 +47,10 @@ int sm_count(int* out);
 int encode_bf16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
                    int box_cols);
 
+// Same for an fp32 matrix (box_cols * 4 bytes == 128), used for TMA stores of logits tiles.
+int encode_f32_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                  int box_cols);
+
 // Opts the kernel into the large dynamic shared memory carve-out (once per device).
 template <class Kernel>
 int ensure_smem_attr(Kernel kernel, std::atomic<uint64_t>& done_mask, int bytes) {
@@ -74,31 +78,88 @@ inline int encode_operand(CUtensorMap* map, const Operand& op, int tile_mn) {
   return encode_bf16_2d(map, op.ptr, op.mn_extent, op.k_extent, op.ld, tile_mn, kBK);
 }
 
+// Which GEMM core runs: the CTA-pair kernel (default) or the single-CTA kernel. The
+// FRX_GEMM_VARIANT environment variable ("pair" / "single") overrides it, for tuning only.
+bool use_pair_kernel();
+
+// Co-resident 2-CTA clusters of `kernel` on the current device (cached per device).
+template <class Kernel>
+int max_pair_clusters(Kernel kernel, std::atomic<int>* cache, int smem_bytes, int* out) {
+  int dev = 0;
+  FRX_CUDA_CHECK(cudaGetDevice(&dev));
+  if (dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) {
+      *out = c;
+      return FRX_OK;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem_bytes);
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  FRX_CUDA_CHECK(cudaOccupancyMaxActiveClusters(&n, kernel, &cfg));
+  FRX_REQUIRE(n >= 1, FRX_ERR_CUDA, "no 2-CTA cluster of the GEMM kernel fits on this device");
+  if (dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+  *out = n;
+  return FRX_OK;
+}
+
 template <bool kAMN, bool kBMN, class Epi>
 int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_t K, int group_m,
                 const typename Epi::Params& ep, int* status, cudaStream_t stream) {
-  static std::atomic<uint64_t> attr_done{0};
+  const bool pair = use_pair_kernel();
+  const int a_rows = kBM;
+  const int b_rows = pair ? kBN / 2 : kBN;
   CUtensorMap tm_a, tm_b;
-  int rc = encode_operand(&tm_a, a, kBM);
+  int rc = encode_operand(&tm_a, a, a_rows);
   if (rc) return rc;
-  rc = encode_operand(&tm_b, b, kBN);
+  rc = encode_operand(&tm_b, b, b_rows);
   if (rc) return rc;
-  auto kernel = gemm_tcgen05_kernel<kAMN, kBMN, Epi>;
-  rc = ensure_smem_attr(kernel, attr_done, kGemmSmemBytes);
-  if (rc) return rc;
-  int sms = 0;
-  rc = sm_count(&sms);
-  if (rc) return rc;
+  const int tile_m = pair ? 2 * kBM : kBM;
   TileSched sched;
-  sched.num_m = static_cast<int>((M + kBM - 1) / kBM);
+  sched.num_m = static_cast<int>((M + tile_m - 1) / tile_m);
   sched.num_n = static_cast<int>((N + kBN - 1) / kBN);
-  sched.group = group_m < 1 ? 1 : (group_m > sched.num_m ? sched.num_m : group_m);
+  const int group = pair ? (group_m + 1) / 2 : group_m;
+  sched.group = group < 1 ? 1 : (group > sched.num_m ? sched.num_m : group);
   const long long tiles = static_cast<long long>(sched.num_m) * sched.num_n;
   FRX_REQUIRE(tiles < (1ll << 31), FRX_ERR_INVALID_ARG, "problem too large: %lld output tiles", tiles);
   sched.num_tiles = static_cast<int>(tiles);
-  const int num_k_blocks = static_cast<int>((K + kBK - 1) / kBK);
-  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  kernel<<<grid, kGemmThreads, kGemmSmemBytes, stream>>>(tm_a, tm_b, sched, num_k_blocks, ep, status);
+  const int stage_k = pair ? kPairBK : kBK;
+  const int num_k_blocks = static_cast<int>((K + stage_k - 1) / stage_k);
+  if (pair) {
+    static std::atomic<uint64_t> attr_done{0};
+    static std::atomic<int> clusters_cache[64];
+    auto kernel = gemm_tcgen05_pair_kernel<kAMN, kBMN, Epi>;
+    constexpr int smem = gemm_smem_bytes(kPairStages * kPairStageBytes, Epi::kSmemBytes);
+    rc = ensure_smem_attr(kernel, attr_done, smem);
+    if (rc) return rc;
+    int clusters = 0;
+    rc = max_pair_clusters(kernel, clusters_cache, smem, &clusters);
+    if (rc) return rc;
+    const long long pairs = tiles < clusters ? tiles : clusters;
+    kernel<<<static_cast<unsigned>(2 * pairs), kGemmThreads, smem, stream>>>(tm_a, tm_b, sched, num_k_blocks, ep,
+                                                                             status);
+  } else {
+    static std::atomic<uint64_t> attr_done{0};
+    auto kernel = gemm_tcgen05_kernel<kAMN, kBMN, Epi>;
+    constexpr int smem = gemm_smem_bytes(kStages * kStageBytes, Epi::kSmemBytes);
+    rc = ensure_smem_attr(kernel, attr_done, smem);
+    if (rc) return rc;
+    int sms = 0;
+    rc = sm_count(&sms);
+    if (rc) return rc;
+    const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+    kernel<<<grid, kGemmThreads, smem, stream>>>(tm_a, tm_b, sched, num_k_blocks, ep, status);
+  }
   FRX_CUDA_CHECK(cudaGetLastError());
   return FRX_OK;
 }
