@@ -47,10 +47,11 @@ def merge_rows(merged_all: Tensor, target_1d: Tensor, vocab_size: int, ignore_in
 
 
 def _gather_stats(local: Tensor, group) -> Tensor:
+    """All-gathers the [rows, 4] per-row statistics of every rank into [world, rows, 4]."""
     world = dist.get_world_size(group)
-    out = torch.empty((world,) + tuple(local.shape), device=local.device, dtype=local.dtype)
+    out = torch.empty((world * local.shape[0],) + tuple(local.shape[1:]), device=local.device, dtype=local.dtype)
     dist.all_gather_into_tensor(out, local.contiguous(), group=group)
-    return out
+    return out.view((world,) + tuple(local.shape))
 
 
 def vocab_parallel_ce_entropy(
