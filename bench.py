@@ -417,8 +417,8 @@ def run_ours(args, world, rank, local):
         try:
             tj = json.loads(tp.read_text())
             ent_ = tj.get("fwd_partials")
-            if ent_ and ent_.get("rows_per_launch") and Vr == ent_.get("vocab_shard", Vr):
-                traffic = ent_["dram_bytes_per_launch"] * rows_per_launch / ent_["rows_per_launch"]
+            if ent_ and ent_.get("rows_per_launch") == rows_per_launch and ent_.get("vocab_shard"):
+                traffic = round(ent_["dram_bytes_per_launch"] * Vr / ent_["vocab_shard"])
         except Exception:
             traffic = None
 
