@@ -118,7 +118,7 @@ extern "C" int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const v
   if (rc) return rc;
   Operand a{dlogits, ld_dlogits, rows, vocab_shard, false};  // [rows, V] row-major, K = V contiguous
   Operand b{weight, ld_weight, hidden_dim, vocab_shard, true};  // [V, H] row-major, N = H contiguous
-  return launch_gemm<false, true, StoreEpilogue>(a, b, rows, hidden_dim, vocab_shard, 8,
+  return launch_gemm<false, true, true, StoreEpilogue>(a, b, rows, hidden_dim, vocab_shard, 8,
                                                  store_params(d_hidden, ld_d_hidden, rows, hidden_dim, out_dtype),
                                                  status, static_cast<cudaStream_t>(stream));
 }
@@ -137,7 +137,7 @@ extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const v
   if (rc) return rc;
   Operand a{dlogits, ld_dlogits, vocab_shard, rows, true};  // [rows, V] row-major, M = V contiguous
   Operand b{hidden, ld_hidden, hidden_dim, rows, true};     // [rows, H] row-major, N = H contiguous
-  return launch_gemm<true, true, StoreEpilogue>(a, b, vocab_shard, hidden_dim, rows, 8,
+  return launch_gemm<true, true, true, StoreEpilogue>(a, b, vocab_shard, hidden_dim, rows, 8,
                                                 store_params(d_weight, ld_d_weight, vocab_shard, hidden_dim, out_dtype),
                                                 status, static_cast<cudaStream_t>(stream));
 }

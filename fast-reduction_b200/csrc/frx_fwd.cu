@@ -186,6 +186,6 @@ extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const voi
   Operand b{weight, ld_weight, vocab_shard, hidden_dim, false};
   // A band of up to 64 row blocks (8192 rows, 64 MiB of bf16 hidden at H=4096) stays in L2
   // while the CTAs sweep the vocabulary.
-  return launch_gemm<false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, 64, ep, status,
+  return launch_gemm<false, false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, 64, ep, status,
                                                        static_cast<cudaStream_t>(stream));
 }

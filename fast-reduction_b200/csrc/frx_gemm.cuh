@@ -47,6 +47,7 @@ struct TileSched {
   int num_n;
   int group;
   int num_tiles;
+  int n256;  // number of 256-column blocks of the output (epilogue bound for wide tiles)
   __device__ __forceinline__ void get(int t, int& m_blk, int& n_blk) const {
     const int per_band = group * num_n;
     const int band = t / per_band;
@@ -238,43 +239,57 @@ namespace frx {
 
 // ---------------------------------------------------------------------------------------------
 // CTA-pair variant (tcgen05 cta_group::2): a cluster of two CTAs on neighbouring SMs computes a
-// 256 x 256 output tile with one M = 256 MMA stream issued by the even CTA. Each CTA stages only
-// its own 128 rows of A and its own 128-row half of B (32 KiB per k-block instead of 48 KiB), so
-// per-SM shared-memory and L2 traffic per FLOP drop by a third against the single-CTA kernel and
-// the ring can be 6 stages deep. Each CTA's TMEM holds the fp32 accumulator of its 128 rows x 256
-// columns, and each CTA runs the epilogue on its own rows. No TMA multicast is used: every CTA
-// loads its own operands; only MMA-completion commits are multicast to both CTAs.
+// 256 x (256 * kNH) output tile with M = 256 MMAs issued by the even CTA. Each CTA stages only its
+// own 128 rows of A and its own 128-row halves of B, so per-SM shared-memory and L2 traffic per
+// FLOP drop by a third against the single-CTA kernel. Each CTA's TMEM holds the fp32 accumulator
+// of its 128 rows, and each CTA runs the epilogue on its own rows. No TMA multicast is used: every
+// CTA loads its own operands; only MMA-completion commits are multicast to both CTAs.
+//
+// Two shapes share the code:
+//   kNH = 1: 256 x 256 tiles, stage K = 128 (two 64-deep sub-tiles per operand), 3 stages, two
+//            256-column TMEM accumulators (tile i's epilogue overlaps tile i+1's mainloop);
+//            used by the forward, whose K (= hidden size) is short.
+//   kNH = 2: 256 x 512 tiles, stage K = 64 with two 256-wide N halves sharing the A sub-tile,
+//            4 stages, one 512-column accumulator; A is re-read half as often, which matters for
+//            the backward GEMMs whose K (= vocabulary or batch) is long enough to hide the
+//            epilogue.
+// Either way a stage is 8 MMAs per tcgen05.commit: every commit costs the tensor pipe a drain
+// bubble of roughly one MMA, which at 4 MMAs per commit held the pipe to ~79% busy and at 8 lets
+// it run at ~99%.
 //
 // Barriers: the even CTA's full[s] counts the bytes of both CTAs' loads (the odd CTA's TMA
 // completes on it through its shared::cluster address); the MMA commit frees empty[s] in both
 // CTAs; acc_full[b] is signalled in both CTAs; the even CTA's acc_empty[b] collects one arrival
 // per epilogue warp of both CTAs.
 // ---------------------------------------------------------------------------------------------
-//
-// Each pipeline stage carries K = 128 (two 64-deep SW128 sub-tiles per operand), i.e. 8 MMAs per
-// tcgen05.commit: every commit costs the tensor pipe a drain bubble of roughly one MMA, which at
-// 4 MMAs per commit held the pipe to ~79% busy and at 8 lets it run at ~99%.
-constexpr int kPairBK = 128;
-constexpr int kPairStages = 3;
-constexpr int kPairSubBytes = 128 * 64 * 2;  // 128 rows x 64 K of bf16, 16 KiB
-constexpr int kPairABytes = 2 * kPairSubBytes;
-constexpr int kPairHalfBBytes = 2 * kPairSubBytes;
-constexpr int kPairStageBytes = kPairABytes + kPairHalfBBytes;
-constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 1024;
+constexpr int kPairSubBytes = 128 * 64 * 2;  // 128 rows x 64 K of bf16 (one SW128 sub-tile), 16 KiB
 
-template <bool kAMN, bool kBMN, class Epi>
+template <int kNH>
+struct PairCfg {
+  static constexpr int kKS = 2 / kNH;                    // 64-deep K sub-tiles per stage
+  static constexpr int kStageK = 64 * kKS;                // K per stage
+  static constexpr int kStages = kNH == 1 ? 3 : 4;
+  static constexpr int kABytes = kKS * kPairSubBytes;     // this CTA's 128 rows of A
+  static constexpr int kBBytes = kKS * kNH * kPairSubBytes;  // this CTA's 128-row slice of each N half
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kNumAcc = 2 / kNH;                 // TMEM accumulator buffers
+  static constexpr int kTileN = 256 * kNH;
+};
+
+template <bool kAMN, bool kBMN, int kNH, class Epi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                              TileSched sched, int num_k_blocks, const __grid_constant__ typename Epi::Params ep,
-                        int* status) {
+                             int* status) {
+  using Cfg = PairCfg<kNH>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_a = smem;
-  uint8_t* s_b = smem + kPairStages * kPairABytes;
-  uint8_t* s_epi = s_b + kPairStages * kPairHalfBBytes;
+  uint8_t* s_b = smem + Cfg::kStages * Cfg::kABytes;
+  uint8_t* s_epi = s_b + Cfg::kStages * Cfg::kBBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(s_epi + Epi::kSmemBytes);
-  uint64_t* empty = full + kPairStages;
-  uint64_t* acc_full = empty + kPairStages;
+  uint64_t* empty = full + Cfg::kStages;
+  uint64_t* acc_full = empty + Cfg::kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -288,7 +303,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const int num_pairs = static_cast<int>(gridDim.x >> 1);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairStages; ++s) {
+    for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -321,39 +336,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       long long issued = 0;
       bool ok = true;
       for (int t = pair_id; t < sched.num_tiles && ok; t += num_pairs) {
-        int pm, n_blk;
-        sched.get(t, pm, n_blk);
+        int pm, pn;
+        sched.get(t, pm, pn);
         const int m0 = pm * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int n0 = n_blk * kBN + static_cast<int>(rank) * (kBN / 2);
+        const int n0 = pn * Cfg::kTileN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < num_k_blocks; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
             ok = false;
             break;
           }
           const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * kPairStageBytes);
-          uint8_t* da = s_a + stage * kPairABytes;
-          uint8_t* db = s_b + stage * kPairHalfBBytes;
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          uint8_t* da = s_a + stage * Cfg::kABytes;
+          uint8_t* db = s_b + stage * Cfg::kBBytes;
 #pragma unroll
-          for (int h = 0; h < kPairBK / 64; ++h) {
-            const int kh = kb * kPairBK + 64 * h;
+          for (int ks = 0; ks < Cfg::kKS; ++ks) {
+            const int kk = kb * Cfg::kStageK + 64 * ks;
+            uint8_t* da_s = da + ks * kPairSubBytes;
             if (kAMN) {
 #pragma unroll
-              for (int g = 0; g < kBM / 64; ++g)
-                tma_load_2d_pair(da + h * kPairSubBytes + g * kMNBoxBytes, &tm_a, bar, m0 + 64 * g, kh);
+              for (int g = 0; g < kBM / 64; ++g) tma_load_2d_pair(da_s + g * kMNBoxBytes, &tm_a, bar, m0 + 64 * g, kk);
             } else {
-              tma_load_2d_pair(da + h * kPairSubBytes, &tm_a, bar, kh, m0);
+              tma_load_2d_pair(da_s, &tm_a, bar, kk, m0);
             }
-            if (kBMN) {
 #pragma unroll
-              for (int g = 0; g < (kBN / 2) / 64; ++g)
-                tma_load_2d_pair(db + h * kPairSubBytes + g * kMNBoxBytes, &tm_b, bar, n0 + 64 * g, kh);
-            } else {
-              tma_load_2d_pair(db + h * kPairSubBytes, &tm_b, bar, kh, n0);
+            for (int h = 0; h < kNH; ++h) {
+              uint8_t* db_s = db + (ks * kNH + h) * kPairSubBytes;
+              const int nh = n0 + 256 * h;
+              if (kBMN) {
+#pragma unroll
+                for (int g = 0; g < 2; ++g) tma_load_2d_pair(db_s + g * kMNBoxBytes, &tm_b, bar, nh + 64 * g, kk);
+              } else {
+                tma_load_2d_pair(db_s, &tm_b, bar, kk, nh);
+              }
             }
           }
           ++issued;
-          if (++stage == kPairStages) {
+          if (++stage == Cfg::kStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -361,9 +380,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       }
       if (!ok) {
         if (leader) {
-          const long long first = issued > kPairStages ? issued - kPairStages : 0;
+          const long long first = issued > Cfg::kStages ? issued - Cfg::kStages : 0;
           for (long long j = first; j < issued; ++j)
-            mbar_wait_drain(&full[j % kPairStages], static_cast<uint32_t>((j / kPairStages) & 1), status);
+            mbar_wait_drain(&full[j % Cfg::kStages], static_cast<uint32_t>((j / Cfg::kStages) & 1), status);
         } else {
           // The odd CTA's copies complete on the even CTA's barriers; give them time to land.
           const uint64_t t0 = global_timer_ns();
@@ -375,42 +394,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (even CTA)
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(2 * kBM, kBN, kAMN, kBMN);
+      constexpr uint32_t idesc = make_idesc_bf16_f32(2 * kBM, 256, kAMN, kBMN);
       constexpr uint32_t a_lbo = kAMN ? kMNBoxBytes : 16;
       constexpr uint32_t b_lbo = kBMN ? kMNBoxBytes : 16;
-      constexpr uint32_t a_kstep = kAMN ? 16 * 128 : 32;
+      constexpr uint32_t a_kstep = kAMN ? 16 * 128 : 32;  // bytes per UMMA_K (= 16) step
       constexpr uint32_t b_kstep = kBMN ? 16 * 128 : 32;
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
       for (int t = pair_id; t < sched.num_tiles && ok; t += num_pairs, ++local) {
-        const int buf = local & 1;
-        const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+        const int buf = local % Cfg::kNumAcc;
+        const uint32_t acc_phase = static_cast<uint32_t>((local / Cfg::kNumAcc) & 1);
         if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, status, kStatusTimeoutMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * 256);
         for (int kb = 0; kb < num_k_blocks; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(s_a + stage * kPairABytes);
-          const uint32_t b_addr = smem_u32(s_b + stage * kPairHalfBBytes);
+          const uint32_t a_addr = smem_u32(s_a + stage * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(s_b + stage * Cfg::kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < kPairBK / 16; ++kk) {
-            const uint32_t sub = static_cast<uint32_t>(kk >> 2) * kPairSubBytes;
-            const uint32_t k = static_cast<uint32_t>(kk & 3);
-            const uint64_t adesc = make_smem_desc_sw128(a_addr + sub + k * a_kstep, a_lbo, 1024);
-            const uint64_t bdesc = make_smem_desc_sw128(b_addr + sub + k * b_kstep, b_lbo, 1024);
-            umma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int ks = 0; ks < Cfg::kKS; ++ks) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t adesc =
+                  make_smem_desc_sw128(a_addr + ks * kPairSubBytes + k * a_kstep, a_lbo, 1024);
+              const uint32_t acc = (kb | ks | k) != 0 ? 1u : 0u;
+#pragma unroll
+              for (int h = 0; h < kNH; ++h) {
+                const uint64_t bdesc =
+                    make_smem_desc_sw128(b_addr + (ks * kNH + h) * kPairSubBytes + k * b_kstep, b_lbo, 1024);
+                umma_bf16_pair(d_tmem + static_cast<uint32_t>(h * 256), adesc, bdesc, idesc, acc);
+              }
+            }
           }
           umma_commit_pair_mc(&empty[stage], 0x3);  // frees this slot in both CTAs
-          if (++stage == kPairStages) {
+          if (++stage == Cfg::kStages) {
             stage = 0;
             phase ^= 1u;
           }
@@ -426,22 +452,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;
     int local = 0;
     for (int t = pair_id; t < sched.num_tiles; t += num_pairs, ++local) {
-      const int buf = local & 1;
-      const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
+      const int buf = local % Cfg::kNumAcc;
+      const uint32_t acc_phase = static_cast<uint32_t>((local / Cfg::kNumAcc) & 1);
       int ok = 1;
       if (lane == 0)
         ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, status, kStatusTimeoutEpilogue) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      int pm, n_blk;
-      sched.get(t, pm, n_blk);
-      const uint32_t tacc = tmem_base + static_cast<uint32_t>(buf * kBN) + (static_cast<uint32_t>(q * 32) << 16);
-      Epi::run(ep, s_epi + q * Epi::kSmemPerWarp, tacc, pm * 2 + static_cast<int>(rank), n_blk, q, lane, [&]() {
+      int pm, pn;
+      sched.get(t, pm, pn);
+      const uint32_t tacc = tmem_base + static_cast<uint32_t>(buf * 256) + (static_cast<uint32_t>(q * 32) << 16);
+      auto release = [&]() {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&acc_empty[buf]), 0));
-      });
+      };
+#pragma unroll 1
+      for (int h = 0; h < kNH; ++h) {
+        const int n_blk = pn * kNH + h;  // 256-column block index
+        const bool last = h == kNH - 1;
+        if (n_blk < sched.n256) {
+          if (last) {
+            Epi::run(ep, s_epi + q * Epi::kSmemPerWarp, tacc + static_cast<uint32_t>(h * 256),
+                     pm * 2 + static_cast<int>(rank), n_blk, q, lane, release);
+          } else {
+            Epi::run(ep, s_epi + q * Epi::kSmemPerWarp, tacc + static_cast<uint32_t>(h * 256),
+                     pm * 2 + static_cast<int>(rank), n_blk, q, lane, [] {});
+          }
+        } else if (last) {
+          release();
+        }
+      }
     }
     Epi::finish(ep, lane);
   }

@@ -113,33 +113,38 @@ int max_pair_clusters(Kernel kernel, std::atomic<int>* cache, int smem_bytes, in
   return FRX_OK;
 }
 
-template <bool kAMN, bool kBMN, class Epi>
+// Launches the GEMM core. kWide selects 256 x 512 pair tiles (backward GEMMs, long K) instead of
+// 256 x 256 double-buffered tiles (forward); it only applies to the pair kernel.
+template <bool kAMN, bool kBMN, bool kWide, class Epi>
 int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_t K, int group_m,
                 const typename Epi::Params& ep, int* status, cudaStream_t stream) {
   const bool pair = use_pair_kernel();
-  const int a_rows = kBM;
-  const int b_rows = pair ? kBN / 2 : kBN;
+  const int b_rows = pair ? 128 : kBN;
   CUtensorMap tm_a, tm_b;
-  int rc = encode_operand(&tm_a, a, a_rows);
+  int rc = encode_operand(&tm_a, a, kBM);
   if (rc) return rc;
   rc = encode_operand(&tm_b, b, b_rows);
   if (rc) return rc;
+  constexpr int kNH = kWide ? 2 : 1;
   const int tile_m = pair ? 2 * kBM : kBM;
+  const int tile_n = pair ? 256 * kNH : kBN;
   TileSched sched;
   sched.num_m = static_cast<int>((M + tile_m - 1) / tile_m);
-  sched.num_n = static_cast<int>((N + kBN - 1) / kBN);
+  sched.num_n = static_cast<int>((N + tile_n - 1) / tile_n);
+  sched.n256 = static_cast<int>((N + 255) / 256);
   const int group = pair ? (group_m + 1) / 2 : group_m;
   sched.group = group < 1 ? 1 : (group > sched.num_m ? sched.num_m : group);
   const long long tiles = static_cast<long long>(sched.num_m) * sched.num_n;
   FRX_REQUIRE(tiles < (1ll << 31), FRX_ERR_INVALID_ARG, "problem too large: %lld output tiles", tiles);
   sched.num_tiles = static_cast<int>(tiles);
-  const int stage_k = pair ? kPairBK : kBK;
-  const int num_k_blocks = static_cast<int>((K + stage_k - 1) / stage_k);
   if (pair) {
+    using Cfg = PairCfg<kNH>;
+    const int num_k_blocks = static_cast<int>((K + Cfg::kStageK - 1) / Cfg::kStageK);
     static std::atomic<uint64_t> attr_done{0};
     static std::atomic<int> clusters_cache[64];
-    auto kernel = gemm_tcgen05_pair_kernel<kAMN, kBMN, Epi>;
-    constexpr int smem = gemm_smem_bytes(kPairStages * kPairStageBytes, Epi::kSmemBytes);
+    auto kernel = gemm_tcgen05_pair_kernel<kAMN, kBMN, kNH, Epi>;
+    constexpr int smem = gemm_smem_bytes(Cfg::kStages * Cfg::kStageBytes, Epi::kSmemBytes);
+    static_assert(smem <= 232448, "shared memory budget exceeded");
     rc = ensure_smem_attr(kernel, attr_done, smem);
     if (rc) return rc;
     int clusters = 0;
@@ -149,9 +154,11 @@ int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_
     kernel<<<static_cast<unsigned>(2 * pairs), kGemmThreads, smem, stream>>>(tm_a, tm_b, sched, num_k_blocks, ep,
                                                                              status);
   } else {
+    const int num_k_blocks = static_cast<int>((K + kBK - 1) / kBK);
     static std::atomic<uint64_t> attr_done{0};
     auto kernel = gemm_tcgen05_kernel<kAMN, kBMN, Epi>;
     constexpr int smem = gemm_smem_bytes(kStages * kStageBytes, Epi::kSmemBytes);
+    static_assert(smem <= 232448, "shared memory budget exceeded");
     rc = ensure_smem_attr(kernel, attr_done, smem);
     if (rc) return rc;
     int sms = 0;
