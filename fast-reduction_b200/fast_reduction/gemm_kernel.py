@@ -29,6 +29,7 @@ Semantics chosen where the reference is inconsistent (documented in DESIGN.md):
 
 from __future__ import annotations
 
+import os
 from typing import Optional, Tuple
 
 import torch
@@ -37,6 +38,20 @@ from torch import Tensor
 from . import ops
 
 IGNORE_INDEX = -100
+
+# Run each chunk's dlogits (HBM-bound) on a side stream so it overlaps the next chunk's forward
+# GEMM (tensor-bound). FRX_OVERLAP_DLOGITS=0 serialises them (for measurement).
+_OVERLAP_DLOGITS = os.environ.get("FRX_OVERLAP_DLOGITS", "1") != "0"
+_side_streams: dict = {}
+
+
+def _side_stream(dev: torch.device) -> torch.cuda.Stream:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _side_streams.get(idx)
+    if st is None:
+        st = torch.cuda.Stream(device=torch.device("cuda", idx))
+        _side_streams[idx] = st
+    return st
 
 
 def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Optional[Tensor]):
@@ -184,22 +199,55 @@ def fwd_bwd_shard(
     chunk = _chunk_rows(chunk_size, B)
     T = ops.n_vocab_tiles(V)
     partials = torch.empty(T, chunk, 4, device=dev, dtype=torch.float32)
-    logits = torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32)
+    n_chunks = (B + chunk - 1) // chunk
+    overlap = _OVERLAP_DLOGITS and n_chunks > 1
+    # Two logits buffers when the dlogits of chunk c (HBM-bound) runs on a side stream under the
+    # forward GEMM of chunk c+1 (tensor-bound); the GEMM of chunk c+2 waits for it.
+    logits_bufs = [torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32)
+                   for _ in range(2 if overlap else 1)]
     dz = torch.empty(B, ops.round_up(V, 8), device=dev, dtype=torch.bfloat16)
-    for start in range(0, B, chunk):
+    main = torch.cuda.current_stream(dev)
+    side = _side_stream(dev) if overlap else None
+    if side is not None:
+        side.wait_stream(main)
+    done = [None, None]
+    for c, start in enumerate(range(0, B, chunk)):
         end = min(start + chunk, B)
         rows = end - start
+        buf = c % len(logits_bufs)
+        logits = logits_bufs[buf]
+        if done[buf] is not None:
+            main.wait_event(done[buf])
         ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
                          logits=logits)
         stats_fn(start, end, partials, T, chunk)
-        ops.dlogits(
-            logits, target_1d[start:end], lse[start:end], entropy[start:end], dz[start:end],
-            rows=rows, vocab_shard=V, ce_weight=ce_weight, ent_weight=ent_weight,
-            g_ce=None if g_ce is None else g_ce[start:end],
-            g_ent=None if g_ent is None else g_ent[start:end],
-            vocab_offset=vocab_offset, ignore_index=ignore_index,
-        )
-    del logits, partials
+
+        def run_dlogits(logits=logits, start=start, end=end, rows=rows):
+            ops.dlogits(
+                logits, target_1d[start:end], lse[start:end], entropy[start:end], dz[start:end],
+                rows=rows, vocab_shard=V, ce_weight=ce_weight, ent_weight=ent_weight,
+                g_ce=None if g_ce is None else g_ce[start:end],
+                g_ent=None if g_ent is None else g_ent[start:end],
+                vocab_offset=vocab_offset, ignore_index=ignore_index,
+            )
+
+        if side is None:
+            run_dlogits()
+        else:
+            ready = torch.cuda.Event()
+            ready.record(main)
+            side.wait_event(ready)
+            with torch.cuda.stream(side):
+                run_dlogits()
+                ev = torch.cuda.Event()
+                ev.record(side)
+            done[buf] = ev
+    if side is not None:
+        main.wait_stream(side)
+        for t_ in logits_bufs + [dz, lse, entropy, target_1d, g_ce, g_ent]:
+            if t_ is not None:
+                t_.record_stream(side)
+    del logits_bufs, partials
     d_hidden = torch.empty(B, H, device=dev, dtype=torch.float32 if dhidden_fp32 else hidden_2d.dtype)
     ops.gemm_dhidden(dz, weight, d_hidden, rows=B, vocab_shard=V)
     pending = dhidden_hook(d_hidden) if dhidden_hook is not None else None
