@@ -47,7 +47,8 @@ constexpr int kFinSplits = 8;
 
 __global__ void __launch_bounds__(kFinRows * kFinSplits)
     finalize_kernel(const float4* __restrict__ partials, int64_t n_tiles, int64_t rows, int64_t tile_stride,
-                    int ref_layout, const int64_t* __restrict__ target, int64_t vocab_size, int64_t ignore_index,
+                    int ref_layout, int ignore_negative, const int64_t* __restrict__ target, int64_t vocab_size,
+                    int64_t ignore_index,
                     float* __restrict__ ce, float* __restrict__ ent, float* __restrict__ lse,
                     float* __restrict__ logp, float4* __restrict__ merged, int* status) {
   __shared__ RowStat red[kFinSplits][kFinRows];
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(kFinRows * kFinSplits)
   float row_ce = row_lse - acc.zt;
   if (target != nullptr) {
     const int64_t t = target[row];
-    if (t == ignore_index) {
+    if (t == ignore_index || (ignore_negative && t < 0)) {
       row_ce = 0.0f;
     } else if (t < 0 || t >= vocab_size) {
       row_ce = __int_as_float(0x7fc00000);
@@ -110,8 +111,8 @@ extern "C" int frx_finalize(const float* partials, int64_t n_tiles, int64_t rows
   FRX_REQUIRE(n_tiles >= 0 && rows >= 0 && tile_stride >= rows, FRX_ERR_INVALID_ARG,
               "frx_finalize: bad sizes n_tiles=%lld rows=%lld tile_stride=%lld", (long long)n_tiles,
               (long long)rows, (long long)tile_stride);
-  FRX_REQUIRE((flags & ~FRX_PARTIALS_REF_LAYOUT) == 0, FRX_ERR_INVALID_ARG, "frx_finalize: unknown flags 0x%x",
-              flags);
+  FRX_REQUIRE((flags & ~(FRX_PARTIALS_REF_LAYOUT | FRX_IGNORE_NEGATIVE_TARGETS)) == 0, FRX_ERR_INVALID_ARG,
+              "frx_finalize: unknown flags 0x%x", flags);
   if (rows == 0) return FRX_OK;
   FRX_REQUIRE(partials != nullptr || n_tiles == 0, FRX_ERR_INVALID_ARG, "frx_finalize: null partials");
   FRX_REQUIRE(partials == nullptr || aligned16(partials), FRX_ERR_INVALID_ARG,
@@ -122,7 +123,7 @@ extern "C" int frx_finalize(const float* partials, int64_t n_tiles, int64_t rows
   FRX_REQUIRE(blocks < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_finalize: too many rows");
   finalize_kernel<<<static_cast<unsigned>(blocks), kFinRows * kFinSplits, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const float4*>(partials), n_tiles, rows, tile_stride, (flags & FRX_PARTIALS_REF_LAYOUT) ? 1 : 0,
-      target, vocab_size, ignore_index, ce, entropy, lse, log_probs, reinterpret_cast<float4*>(merged), status);
+      (flags & FRX_IGNORE_NEGATIVE_TARGETS) ? 1 : 0, target, vocab_size, ignore_index, ce, entropy, lse, log_probs, reinterpret_cast<float4*>(merged), status);
   FRX_CUDA_CHECK(cudaGetLastError());
   return FRX_OK;
 }

@@ -1,0 +1,191 @@
+// Softmax partials of given logits (no GEMM): the standalone cross-entropy / entropy /
+// logsumexp reductions over a materialised [rows, cols] logits matrix.
+//
+// One CTA reduces one (row, column tile) to the same (m, s, u, zt) partial the fused GEMM
+// epilogue writes, so frx_finalize produces ce / entropy / lse from it, and a long row is
+// spread over several CTAs when there are few rows. Each thread streams 16-byte vectors and
+// keeps an online (max, sum exp, sum (x - max) exp) over them; the CTA merges its 8 warps.
+// HBM-bound: cols * sizeof(T) bytes read per row.
+// Reference: fast_reduction/cute_cross_entropy.py:171-578 (CrossEntropyOnly, EntropyOnly,
+// CrossEntropyEntropy), wrappers :583-735.
+#include <cuda_fp16.h>
+
+#include "frx_host.cuh"
+
+namespace frx {
+
+constexpr int kRowThreads = 256;
+
+struct OnlineStat {
+  float m, s, u;
+};
+
+__device__ __forceinline__ void online_merge(OnlineStat& a, const OnlineStat& b) {
+  if (b.m == -INFINITY) return;
+  if (a.m == -INFINITY) {
+    a = b;
+    return;
+  }
+  const float M = fmaxf(a.m, b.m);
+  const float da = a.m - M, db = b.m - M;
+  const float ea = ex2_approx(da * kLog2e), eb = ex2_approx(db * kLog2e);
+  a.u = fmaf(da, a.s, a.u) * ea + fmaf(db, b.s, b.u) * eb;
+  a.s = a.s * ea + b.s * eb;
+  a.m = M;
+}
+
+template <int N>
+__device__ __forceinline__ void online_add(OnlineStat& st, const float (&v)[N], int n_valid) {
+  float vm = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < N; ++i)
+    if (i < n_valid) vm = fmaxf(vm, v[i]);
+  if (vm == -INFINITY) return;
+  OnlineStat b{vm, 0.f, 0.f};
+  const float ml = vm * kLog2e;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    if (i < n_valid) {
+      const float e = ex2_approx(fmaf(v[i], kLog2e, -ml));
+      b.s += e;
+      b.u = fmaf(v[i] - vm, e, b.u);
+    }
+  }
+  online_merge(st, b);
+}
+
+template <typename T>
+struct Vec16;
+template <>
+struct Vec16<float> {
+  static constexpr int N = 4;
+  __device__ static void load(const float* p, float (&v)[4]) {
+    const float4 q = __ldcs(reinterpret_cast<const float4*>(p));
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+  }
+  __device__ static float scalar(const float* p) { return *p; }
+};
+template <>
+struct Vec16<__nv_bfloat16> {
+  static constexpr int N = 8;
+  __device__ static void load(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 q = __ldcs(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+  __device__ static float scalar(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+};
+template <>
+struct Vec16<__half> {
+  static constexpr int N = 8;
+  __device__ static void load(const __half* p, float (&v)[8]) {
+    const uint4 q = __ldcs(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  }
+  __device__ static float scalar(const __half* p) { return __half2float(*p); }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads)
+    logits_partials_kernel(const T* __restrict__ x, int64_t ld, int64_t rows, int64_t cols,
+                           const int64_t* __restrict__ target, int64_t tile_cols, float4* __restrict__ partials,
+                           int64_t tile_stride, int vec_ok) {
+  using V = Vec16<T>;
+  constexpr int N = V::N;
+  __shared__ OnlineStat red[kRowThreads / 32];
+  const int64_t tile = blockIdx.x;
+  const int64_t c_begin = tile * tile_cols;
+  const int64_t c_end = min(cols, c_begin + tile_cols);
+  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+    const T* xr = x + row * ld;
+    OnlineStat st{-INFINITY, 0.f, 0.f};
+    if (vec_ok) {
+      for (int64_t c = c_begin + static_cast<int64_t>(threadIdx.x) * N; c < c_end;
+           c += static_cast<int64_t>(kRowThreads) * N) {
+        float v[N];
+        if (c + N <= c_end) {
+          V::load(xr + c, v);
+          online_add<N>(st, v, N);
+        } else {
+#pragma unroll
+          for (int i = 0; i < N; ++i) v[i] = (c + i < c_end) ? V::scalar(xr + c + i) : 0.f;
+          online_add<N>(st, v, static_cast<int>(c_end - c));
+        }
+      }
+    } else {
+      for (int64_t c = c_begin + threadIdx.x; c < c_end; c += kRowThreads) {
+        float v[1] = {V::scalar(xr + c)};
+        online_add<1>(st, v, 1);
+      }
+    }
+    // warp merge, then across warps
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      OnlineStat o{__shfl_xor_sync(0xffffffffu, st.m, off), __shfl_xor_sync(0xffffffffu, st.s, off),
+                   __shfl_xor_sync(0xffffffffu, st.u, off)};
+      online_merge(st, o);
+    }
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = st;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < kRowThreads / 32; ++w) online_merge(st, red[w]);
+      float zt = 0.f;
+      if (target != nullptr) {
+        const int64_t t = target[row];
+        if (t >= c_begin && t < c_end) zt = V::scalar(xr + t);
+      }
+      partials[tile * tile_stride + row] = make_float4(st.m, st.s, st.u, zt);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace frx
+
+extern "C" int frx_logits_partials(const void* logits, int dtype, int64_t ld, int64_t rows, int64_t cols,
+                                   const int64_t* target, int64_t tile_cols, float* partials, int64_t tile_stride,
+                                   void* stream) {
+  using namespace frx;
+  FRX_REQUIRE(rows >= 0 && cols >= 1 && tile_cols >= 1 && ld >= cols && tile_stride >= rows, FRX_ERR_INVALID_ARG,
+              "frx_logits_partials: bad sizes rows=%lld cols=%lld ld=%lld tile_cols=%lld tile_stride=%lld",
+              (long long)rows, (long long)cols, (long long)ld, (long long)tile_cols, (long long)tile_stride);
+  if (rows == 0) return FRX_OK;
+  FRX_REQUIRE(logits != nullptr && partials != nullptr && aligned16(partials), FRX_ERR_INVALID_ARG,
+              "frx_logits_partials: null logits/partials or unaligned partials");
+  const int64_t n_tiles = (cols + tile_cols - 1) / tile_cols;
+  FRX_REQUIRE(n_tiles < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_logits_partials: too many tiles");
+  const dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(rows < 65535 ? rows : 65535));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == FRX_DTYPE_F32) {
+    const int vec_ok = aligned16(logits) && ld % 4 == 0 && tile_cols % 4 == 0;
+    logits_partials_kernel<float><<<grid, kRowThreads, 0, st>>>(static_cast<const float*>(logits), ld, rows, cols,
+                                                                 target, tile_cols,
+                                                                 reinterpret_cast<float4*>(partials), tile_stride,
+                                                                 vec_ok);
+  } else if (dtype == FRX_DTYPE_BF16) {
+    const int vec_ok = aligned16(logits) && ld % 8 == 0 && tile_cols % 8 == 0;
+    logits_partials_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(logits), ld, rows, cols, target, tile_cols,
+        reinterpret_cast<float4*>(partials), tile_stride, vec_ok);
+  } else if (dtype == FRX_DTYPE_F16) {
+    const int vec_ok = aligned16(logits) && ld % 8 == 0 && tile_cols % 8 == 0;
+    logits_partials_kernel<__half><<<grid, kRowThreads, 0, st>>>(static_cast<const __half*>(logits), ld, rows, cols,
+                                                                  target, tile_cols,
+                                                                  reinterpret_cast<float4*>(partials), tile_stride,
+                                                                  vec_ok);
+  } else {
+    FRX_REQUIRE(false, FRX_ERR_INVALID_ARG, "frx_logits_partials: unknown dtype %d", dtype);
+  }
+  FRX_CUDA_CHECK(cudaGetLastError());
+  return FRX_OK;
+}

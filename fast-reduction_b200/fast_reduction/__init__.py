@@ -9,6 +9,7 @@ sm_100a behind a C ABI, include/frx.h); there is no CPU or library fallback.
 __all__ = [
     "gemm_fused_ce_entropy",
     "gemm_fused_ce_entropy_v2",
+    "gemm_fused_ce_entropy_differentiable",
     "gemm_fused_ce_entropy_fast",
     "gemm_megakernel_fast",
     "vocab_parallel_ce_entropy",
@@ -18,6 +19,7 @@ __all__ = [
 _GEMM_KERNEL_NAMES = {
     "gemm_fused_ce_entropy",
     "gemm_fused_ce_entropy_v2",
+    "gemm_fused_ce_entropy_differentiable",
     "gemm_fused_ce_entropy_fast",
     "gemm_megakernel_fast",
 }

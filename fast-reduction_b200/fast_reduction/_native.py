@@ -23,9 +23,11 @@ FRX_ERR_CUDA = 3
 
 FRX_DTYPE_BF16 = 0
 FRX_DTYPE_F32 = 1
+FRX_DTYPE_F16 = 2
 
 FRX_VOCAB_TILE = 256
 FRX_PARTIALS_REF_LAYOUT = 1
+FRX_IGNORE_NEGATIVE_TARGETS = 2
 
 FRX_STATUS_TIMEOUT_PRODUCER = 1
 FRX_STATUS_TIMEOUT_MMA = 2
@@ -58,6 +60,7 @@ SIGNATURES: dict[str, tuple] = {
     "frx_gemm_dhidden": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
     "frx_gemm_dweight": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
     "frx_fwd_ce_entropy_noalloc": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
+    "frx_logits_partials": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P]),
 }
 
 _lib = None

@@ -158,6 +158,72 @@ def gemm_fused_ce_entropy(
     return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
 
 
+class GemmFusedCEEntropy(torch.autograd.Function):
+    """Differentiable forward (reference GemmFusedCEEntropy, gemm_kernel.py:541-568).
+
+    Forward: the GEMM-epilogue path (no logits in HBM); saves the per-row lse and entropy.
+    Backward(g_ce, g_ent, g_lp): arbitrary per-row upstream gradients; since log_probs = -ce,
+    the CE weight is g_ce - g_lp (reference :559-562). The logits are recomputed chunk by chunk by
+    the same deterministic GEMM (bitwise equal to the forward's), turned into bf16 dlogits with
+    the per-row weights, and fed to the d_hidden / d_weight GEMMs.
+    """
+
+    @staticmethod
+    def forward(ctx, hidden_states, weight, target, bias, chunk_size):
+        batch_shape, hidden_2d, weight_c, target_1d = _prepare(hidden_states, weight, target, bias)
+        B = hidden_2d.shape[0]
+        dev = hidden_2d.device
+        ce = torch.empty(B, device=dev, dtype=torch.float32)
+        ent = torch.empty(B, device=dev, dtype=torch.float32)
+        lse = torch.empty(B, device=dev, dtype=torch.float32)
+        logp = torch.empty(B, device=dev, dtype=torch.float32)
+        forward_stats(hidden_2d, weight_c, target_1d, chunk_size, ce=ce, entropy=ent, lse=lse, log_probs=logp)
+        ctx.save_for_backward(hidden_2d, weight_c, target_1d, lse, ent)
+        ctx.chunk_size = chunk_size
+        ctx.hidden_shape = hidden_states.shape
+        return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
+
+    @staticmethod
+    def backward(ctx, g_ce, g_ent, g_lp):
+        hidden_2d, weight, target_1d, lse, ent = ctx.saved_tensors
+        B = hidden_2d.shape[0]
+        dev = hidden_2d.device
+        zeros = None
+
+        def per_row(g):
+            nonlocal zeros
+            if g is None:
+                if zeros is None:
+                    zeros = torch.zeros(B, device=dev, dtype=torch.float32)
+                return zeros
+            return g.reshape(-1).to(torch.float32).contiguous()
+
+        gce = per_row(g_ce)
+        if g_lp is not None:
+            gce = gce - per_row(g_lp)
+        gent = per_row(g_ent)
+        if B == 0:
+            return torch.zeros(ctx.hidden_shape, device=dev, dtype=hidden_2d.dtype), torch.zeros_like(weight), \
+                None, None, None
+        d_hidden, d_weight, _ = fwd_bwd_shard(
+            hidden_2d, weight, target_1d, ctx.chunk_size, 0.0, 0.0, lse=lse, entropy=ent,
+            ignore_index=IGNORE_INDEX, stats_fn=lambda *args: None, g_ce=gce, g_ent=gent,
+        )
+        return d_hidden.view(ctx.hidden_shape), d_weight, None, None, None
+
+
+def gemm_fused_ce_entropy_differentiable(
+    hidden_states: Tensor,
+    weight: Tensor,
+    target: Tensor,
+    bias: Optional[Tensor] = None,
+    chunk_size: int = 4096,
+) -> Tuple[Tensor, Tensor, Tensor]:
+    """Differentiable gemm_fused_ce_entropy: (ce_loss, entropy, log_probs) that support
+    .backward() with any per-row upstream gradients (reference gemm_kernel.py:571-582)."""
+    return GemmFusedCEEntropy.apply(hidden_states, weight, target, bias, chunk_size)
+
+
 # The reference's two-pass epilogue variant (Level 5.2, gemm_kernel.py:363-534) exists for
 # precision: no online merge inside a CTA tile. The sm_100a epilogue already reduces each
 # 256-column tile in two passes against the exact tile max, so both names run the same engine.

@@ -112,6 +112,7 @@ def finalize(
     tile_stride: int,
     *,
     ref_layout: bool = False,
+    ignore_negative: bool = False,
     target: torch.Tensor | None = None,
     vocab_size: int = 0,
     ignore_index: int = NO_IGNORE,
@@ -136,7 +137,8 @@ def finalize(
         raise ValueError("target must be a contiguous int64 tensor with one id per row")
     lib = nat.load()
     rc = _launch("finalize", dev, lambda: lib.frx_finalize(
-        partials.data_ptr(), n_tiles, rows, tile_stride, nat.FRX_PARTIALS_REF_LAYOUT if ref_layout else 0,
+        partials.data_ptr(), n_tiles, rows, tile_stride,
+        (nat.FRX_PARTIALS_REF_LAYOUT if ref_layout else 0) | (nat.FRX_IGNORE_NEGATIVE_TARGETS if ignore_negative else 0),
         nat.ptr(target), vocab_size, ignore_index, nat.ptr(ce), nat.ptr(entropy), nat.ptr(lse), nat.ptr(log_probs),
         nat.ptr(merged), nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
@@ -231,3 +233,27 @@ def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, r
         nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_gemm_dweight")
+
+
+_LOGITS_DTYPES = {torch.bfloat16: nat.FRX_DTYPE_BF16, torch.float16: nat.FRX_DTYPE_F16, torch.float32: nat.FRX_DTYPE_F32}
+
+
+def logits_partials(logits: torch.Tensor, target: torch.Tensor | None, partials: torch.Tensor, tile_cols: int,
+                    tile_stride: int) -> None:
+    """partials[t, r] <- (m, s, u, zt) of logits[r, t*tile_cols : (t+1)*tile_cols] (any float dtype)."""
+    dev = _require_cuda(logits, target, partials)
+    ld = _row_major(logits, "logits")
+    if logits.dtype not in _LOGITS_DTYPES:
+        raise TypeError(f"logits must be bfloat16, float16 or float32, got {logits.dtype}")
+    rows, cols = logits.shape
+    if target is not None and (target.dtype != torch.int64 or not target.is_contiguous() or target.numel() < rows):
+        raise ValueError("target must be a contiguous int64 tensor with one id per row")
+    n_tiles = (cols + tile_cols - 1) // tile_cols
+    if partials.dtype != torch.float32 or not partials.is_contiguous() or partials.numel() < 4 * n_tiles * tile_stride:
+        raise ValueError("partials must be contiguous float32 with n_tiles * tile_stride float4")
+    lib = nat.load()
+    rc = _launch("logits_partials", dev, lambda: lib.frx_logits_partials(
+        logits.data_ptr(), _LOGITS_DTYPES[logits.dtype], ld, rows, cols, nat.ptr(target), tile_cols,
+        partials.data_ptr(), tile_stride, nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_logits_partials")

@@ -46,12 +46,14 @@ extern "C" {
 
 #define FRX_DTYPE_BF16 0
 #define FRX_DTYPE_F32 1
+#define FRX_DTYPE_F16 2
 
 /* Width of one vocabulary tile of the forward partials (columns per partial). */
 #define FRX_VOCAB_TILE 256
 
 /* frx_finalize flags */
 #define FRX_PARTIALS_REF_LAYOUT 1 /* third slot holds sum z*exp(z-m) (reference layout) */
+#define FRX_IGNORE_NEGATIVE_TARGETS 2 /* every target < 0 is ignored (ce = log_probs = 0) */
 
 /* device status bits */
 #define FRX_STATUS_TIMEOUT_PRODUCER 1
@@ -92,7 +94,9 @@ FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* 
  *
  *   lse = M + log S,  entropy = log S - U / S,  ce = lse - ZT,  log_probs = -ce
  * Rows whose target equals ignore_index get ce = 0 and log_probs = 0 (torch nll_loss
- * semantics); targets outside [0, vocab_size) give NaN and set FRX_STATUS_BAD_TARGET.
+ * semantics), or, with FRX_IGNORE_NEGATIVE_TARGETS, every row whose target is negative (the rule
+ * of the reference's standalone reductions); other targets outside [0, vocab_size) give NaN and
+ * set FRX_STATUS_BAD_TARGET.
  * target may be NULL (no CE semantics check). Any of ce/entropy/lse/log_probs may be NULL.
  * `merged` (optional, float4 per row) receives the merged (M, S, U, ZT) in the u layout, for a
  * further cross-shard merge (call frx_finalize again with n_tiles = number of shards).
@@ -131,6 +135,19 @@ FRX_API int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void
 FRX_API int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
                      void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
                      int64_t hidden_dim, int64_t rows, int* status, void* stream);
+
+/*
+ * Softmax partials of a materialised logits matrix [rows, cols] (dtype FRX_DTYPE_BF16, _F16 or
+ * _F32, row stride ld elements): for each tile of tile_cols columns and each row, the same
+ * (m, s, u, zt) float4 as frx_fwd_partials writes (zt = logits[row, target] when the target lies in
+ * the tile), at partials[tile * tile_stride + row]; frx_finalize then gives ce / entropy / lse.
+ * Replaces the reference's standalone row reductions CrossEntropyOnly / EntropyOnly /
+ * CrossEntropyEntropy and their custom ops ce_fwd / entropy_fwd / ce_entropy_fwd[_lse]
+ * (fast_reduction/cute_cross_entropy.py:171-578, 583-735). target may be NULL.
+ */
+FRX_API int frx_logits_partials(const void* logits, int dtype, int64_t ld, int64_t rows, int64_t cols,
+                                const int64_t* target, int64_t tile_cols, float* partials, int64_t tile_stride,
+                                void* stream);
 
 /*
  * Forward CE / entropy / lse / log_probs in one call that allocates no device memory: the

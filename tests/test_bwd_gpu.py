@@ -191,3 +191,41 @@ def test_megakernel_chunked_equals_unchunked_and_dloss_scaling():
     assert torch.equal(grads[0][1], grads[1][1])
     torch.testing.assert_close(grads[2][0].float(), 3.0 * grads[0][0].float(), atol=1e-6, rtol=1e-2)
     torch.testing.assert_close(grads[2][1].float(), 3.0 * grads[0][1].float(), atol=1e-6, rtol=1e-2)
+
+
+def test_differentiable_matches_fp32_with_per_row_upstream_grads():
+    """gemm_fused_ce_entropy_differentiable (reference gemm_kernel.py:541-582): backward with
+    arbitrary per-row g_ce, g_ent and g_lp (log_probs = -ce, so the CE weight is g_ce - g_lp)."""
+    from fast_reduction.gemm_kernel import gemm_fused_ce_entropy_differentiable
+
+    h, w, t = rm.make_inputs(300, 128, 1000, seed=21, weight_std=0.3, ignore_frac=0.05)
+    hd = h.to(DEV).requires_grad_(True)
+    wd = w.to(DEV).requires_grad_(True)
+    ce, ent, lp = gemm_fused_ce_entropy_differentiable(hd, wd, t.to(DEV), chunk_size=128)
+    g = torch.Generator().manual_seed(5)
+    gce, gent, glp = (torch.randn(300, generator=g) for _ in range(3))
+    (ce * gce.to(DEV)).sum().backward(retain_graph=True)
+    ((ent * gent.to(DEV)).sum() + (lp * glp.to(DEV)).sum()).backward()
+    ce_ref, ent_ref, dh_ref, dw_ref = rm.fp32_reference_grads(h, w, t, g_ce=gce - glp, g_ent=gent)
+    torch.testing.assert_close(ce.detach().cpu(), ce_ref, atol=2e-3, rtol=1e-3)
+    rel_dh = (hd.grad.float().cpu() - dh_ref).norm() / dh_ref.norm()
+    rel_dw = (wd.grad.float().cpu() - dw_ref).norm() / dw_ref.norm()
+    assert rel_dh < 1e-2 and rel_dw < 1e-2, (rel_dh, rel_dw)
+
+
+def test_differentiable_default_weights_match_megakernel():
+    """With g_ce = 1, g_ent = -1 the differentiable path and the megakernel give the same gradients
+    (same logits, same dlogits formula; only the order of chunk recomputation differs)."""
+    from fast_reduction.gemm_kernel import gemm_fused_ce_entropy_differentiable, gemm_megakernel_fast
+
+    h, w, t = rm.make_inputs(256, 128, 1024, seed=22, weight_std=0.2)
+    h1 = h.to(DEV).requires_grad_(True)
+    w1 = w.to(DEV).requires_grad_(True)
+    ce, ent, _ = gemm_fused_ce_entropy_differentiable(h1, w1, t.to(DEV), chunk_size=100)
+    (ce.sum() - ent.sum()).backward()
+    h2 = h.to(DEV).requires_grad_(True)
+    w2 = w.to(DEV).requires_grad_(True)
+    loss, _, _ = gemm_megakernel_fast(h2, w2, t.to(DEV), chunk_size=100)
+    loss.backward()
+    assert torch.equal(h1.grad, h2.grad)
+    assert torch.equal(w1.grad, w2.grad)
