@@ -8,7 +8,8 @@
 //   pass 2: s = sum exp(z - m) and u = sum (z - m) exp(z - m) against that exact tile max.
 // The reference computes the same four numbers per (row, 256-column tile) in
 // fast_reduction/gemm_ce_entropy_epilogue.py:184-271 (its third slot is sum z exp(z - m)).
-// Columns at or beyond the shard's vocabulary size are skipped, not sentinel-filled.
+// Columns at or beyond the shard's vocabulary size are skipped, not sentinel-filled. An optional
+// bf16 bias is added to each column before the reductions (and before the logits store).
 #include <cstring>
 
 #include "frx_host.cuh"
@@ -30,6 +31,26 @@ __device__ __forceinline__ float select32(const float (&v)[32], int idx) {
   return (idx & 1) ? w2[1] : w2[0];
 }
 
+// v[j] += bias[j] for the valid columns of a 32-column chunk (bf16 bias, fp32 add).
+__device__ __forceinline__ void add_bias32(float (&v)[32], const __nv_bfloat16* b, int lim, bool vec) {
+  if (lim >= 32 && vec) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4*>(b) + q);
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[8 * q + 2 * i] += __uint_as_float(u[i] << 16);
+        v[8 * q + 2 * i + 1] += __uint_as_float(u[i] & 0xFFFF0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < lim) v[j] += __bfloat162float(b[j]);
+  }
+}
+
 struct CEPartialsEpilogue {
   // Two 32 x 32 fp32 staging blocks per epilogue warp for the optional logits store.
   static constexpr int kSmemPerWarp = 2 * 32 * 32 * 4;
@@ -38,12 +59,14 @@ struct CEPartialsEpilogue {
   struct Params {
     CUtensorMap tm_logits;  // fp32 [rows, vocab_shard] logits, 32 x 32 boxes, 128B swizzle
     const int64_t* target;
+    const __nv_bfloat16* bias;  // optional [vocab_shard] bias of this shard
     int64_t vocab_offset;
     int rows;
     int vocab_shard;
     float4* partials;
     int64_t tile_stride;
     int has_logits;
+    int bias_vec;  // bias base 16-byte aligned
   };
 
   template <class Release>
@@ -70,6 +93,7 @@ struct CEPartialsEpilogue {
       if (lim <= 0) break;
       __syncwarp();  // tcgen05.ld is warp-collective: reconverge after per-row branches
       tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
+      if (p.bias != nullptr) add_bias32(v, p.bias + n0 + c * 32, lim, p.bias_vec != 0);
       if (lim >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
@@ -111,6 +135,7 @@ struct CEPartialsEpilogue {
       if (lim <= 0) break;
       __syncwarp();
       tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
+      if (p.bias != nullptr) add_bias32(v, p.bias + n0 + c * 32, lim, p.bias_vec != 0);
       if (lim >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
@@ -146,7 +171,8 @@ struct CEPartialsEpilogue {
 }  // namespace frx
 
 extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
-                                const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
+                                const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
+                                int64_t hidden_dim,
                                 int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
                                 int64_t ld_logits, int* status, void* stream) {
   using namespace frx;
@@ -177,6 +203,8 @@ extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const voi
     ep.has_logits = 1;
   }
   ep.target = target;
+  ep.bias = static_cast<const __nv_bfloat16*>(bias);
+  ep.bias_vec = aligned16(bias) ? 1 : 0;
   ep.vocab_offset = vocab_offset;
   ep.rows = static_cast<int>(rows);
   ep.vocab_shard = static_cast<int>(vocab_shard);

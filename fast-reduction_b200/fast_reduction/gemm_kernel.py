@@ -20,8 +20,10 @@ Engine (all device work is libfrx, sm_100a):
 Semantics chosen where the reference is inconsistent (documented in DESIGN.md):
   * ignore_index (default -100): ce = 0, log_probs = 0 and no CE gradient for such rows; the
     entropy and its gradient are kept (torch nll_loss semantics, reference baseline.py:80).
-  * bias: the reference accepts it but never adds it to the logits (gemm_kernel.py:280);
-    here a non-None bias raises NotImplementedError.
+  * bias: the reference accepts it but never adds it to the logits in its GEMM path
+    (gemm_kernel.py:280) while its fp32 baseline does (baseline.py:76); here a bias [V] (dtype of
+    the weight) is added to every logit in the GEMM epilogue, and its gradient is the column sum
+    of dlogits (the reference's `d_bias.add_(dlogits.sum(dim=0))`, gemm_kernel.py:867-869).
   * loss = ce_weight * sum(ce) + ent_weight * sum(entropy) (a sum, gemm_kernel.py:897).
   * tile_M / tile_N are accepted for signature compatibility and ignored (tiles are fixed at
     128 x 256 by the sm_100a kernel; the partials use 256-column vocabulary tiles).
@@ -55,8 +57,6 @@ def _side_stream(dev: torch.device) -> torch.cuda.Stream:
 
 
 def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Optional[Tensor]):
-    if bias is not None:
-        raise NotImplementedError("bias is not supported by the B200 engine (the reference ignores it in the forward)")
     if hidden_states.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
         raise NotImplementedError(
             f"the B200 engine computes in bf16; got hidden {hidden_states.dtype}, weight {weight.dtype}"
@@ -82,8 +82,14 @@ def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Option
             raise TypeError(f"target must be an integer tensor, got {target_1d.dtype}")
         target_1d = target_1d.to(torch.int64)
     target_1d = target_1d.contiguous()
-    ops._require_cuda(hidden_2d, weight, target_1d)
-    return batch_shape, hidden_2d, weight, target_1d
+    if bias is not None:
+        if bias.dim() != 1 or bias.numel() != weight.shape[0]:
+            raise ValueError(f"bias must be [V={weight.shape[0]}], got shape {tuple(bias.shape)}")
+        if bias.dtype != torch.bfloat16:
+            raise NotImplementedError(f"bias must be bf16 like the weight, got {bias.dtype}")
+        bias = bias.contiguous()
+    ops._require_cuda(hidden_2d, weight, target_1d, bias)
+    return batch_shape, hidden_2d, weight, target_1d, bias
 
 
 def _chunk_rows(chunk_size: int, B: int) -> int:
@@ -106,6 +112,7 @@ def forward_stats(
     merged: Optional[Tensor] = None,
     vocab_size: Optional[int] = None,
     ignore_index: int = IGNORE_INDEX,
+    bias: Optional[Tensor] = None,
 ) -> None:
     """Forward over one vocabulary shard, chunked over rows: GEMM-epilogue partials + finalize.
 
@@ -123,7 +130,8 @@ def forward_stats(
     for start in range(0, B, chunk):
         end = min(start + chunk, B)
         rows = end - start
-        ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset)
+        ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
+                         bias=bias)
         ops.finalize(
             partials, T, rows, chunk,
             target=target_1d[start:end], vocab_size=vocab_size, ignore_index=ignore_index,
@@ -147,14 +155,14 @@ def gemm_fused_ce_entropy(
 ) -> Tuple[Tensor, Tensor, Tensor]:
     """Fused linear + CE + entropy forward. Returns (ce_loss, entropy, log_probs), each fp32
     and shaped like ``hidden_states.shape[:-1]``. The [chunk, V] logits never reach HBM."""
-    batch_shape, hidden_2d, weight, target_1d = _prepare(hidden_states, weight, target, bias)
+    batch_shape, hidden_2d, weight, target_1d, bias = _prepare(hidden_states, weight, target, bias)
     B = hidden_2d.shape[0]
     dev = hidden_2d.device
     ce = torch.empty(B, device=dev, dtype=torch.float32)
     ent = torch.empty(B, device=dev, dtype=torch.float32)
     logp = torch.empty(B, device=dev, dtype=torch.float32)
     forward_stats(hidden_2d, weight, target_1d, chunk_size, ce=ce, entropy=ent, log_probs=logp,
-                  ignore_index=ignore_index)
+                  ignore_index=ignore_index, bias=bias)
     return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
 
 
@@ -170,22 +178,23 @@ class GemmFusedCEEntropy(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, hidden_states, weight, target, bias, chunk_size):
-        batch_shape, hidden_2d, weight_c, target_1d = _prepare(hidden_states, weight, target, bias)
+        batch_shape, hidden_2d, weight_c, target_1d, bias_c = _prepare(hidden_states, weight, target, bias)
         B = hidden_2d.shape[0]
         dev = hidden_2d.device
         ce = torch.empty(B, device=dev, dtype=torch.float32)
         ent = torch.empty(B, device=dev, dtype=torch.float32)
         lse = torch.empty(B, device=dev, dtype=torch.float32)
         logp = torch.empty(B, device=dev, dtype=torch.float32)
-        forward_stats(hidden_2d, weight_c, target_1d, chunk_size, ce=ce, entropy=ent, lse=lse, log_probs=logp)
-        ctx.save_for_backward(hidden_2d, weight_c, target_1d, lse, ent)
+        forward_stats(hidden_2d, weight_c, target_1d, chunk_size, ce=ce, entropy=ent, lse=lse, log_probs=logp,
+                      bias=bias_c)
+        ctx.save_for_backward(hidden_2d, weight_c, target_1d, lse, ent, bias_c)
         ctx.chunk_size = chunk_size
         ctx.hidden_shape = hidden_states.shape
         return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
 
     @staticmethod
     def backward(ctx, g_ce, g_ent, g_lp):
-        hidden_2d, weight, target_1d, lse, ent = ctx.saved_tensors
+        hidden_2d, weight, target_1d, lse, ent, bias = ctx.saved_tensors
         B = hidden_2d.shape[0]
         dev = hidden_2d.device
         zeros = None
@@ -203,13 +212,13 @@ class GemmFusedCEEntropy(torch.autograd.Function):
             gce = gce - per_row(g_lp)
         gent = per_row(g_ent)
         if B == 0:
-            return torch.zeros(ctx.hidden_shape, device=dev, dtype=hidden_2d.dtype), torch.zeros_like(weight), \
-                None, None, None
-        d_hidden, d_weight, _ = fwd_bwd_shard(
+            return (torch.zeros(ctx.hidden_shape, device=dev, dtype=hidden_2d.dtype), torch.zeros_like(weight), None,
+                    None if bias is None else torch.zeros_like(bias), None)
+        d_hidden, d_weight, d_bias, _ = fwd_bwd_shard(
             hidden_2d, weight, target_1d, ctx.chunk_size, 0.0, 0.0, lse=lse, entropy=ent,
-            ignore_index=IGNORE_INDEX, stats_fn=lambda *args: None, g_ce=gce, g_ent=gent,
+            ignore_index=IGNORE_INDEX, stats_fn=lambda *args: None, g_ce=gce, g_ent=gent, bias=bias,
         )
-        return d_hidden.view(ctx.hidden_shape), d_weight, None, None, None
+        return d_hidden.view(ctx.hidden_shape), d_weight, None, d_bias, None
 
 
 def gemm_fused_ce_entropy_differentiable(
@@ -247,11 +256,12 @@ def fwd_bwd_shard(
     g_ent: Optional[Tensor] = None,
     dhidden_fp32: bool = False,
     dhidden_hook=None,
+    bias: Optional[Tensor] = None,
 ):
-    """Training pass over one vocabulary shard; returns (d_hidden [B, H], d_weight [V_shard, H], pending)
-    where d_hidden is this shard's contribution (fp32 if ``dhidden_fp32``) and ``pending`` is what
-    ``dhidden_hook(d_hidden)`` returned (it runs between the d_hidden and d_weight GEMMs, so a
-    cross-shard reduction can overlap the d_weight GEMM), or None.
+    """Training pass over one vocabulary shard; returns (d_hidden [B, H], d_weight [V_shard, H],
+    d_bias [V_shard] or None, pending) where d_hidden is this shard's contribution (fp32 if
+    ``dhidden_fp32``) and ``pending`` is what ``dhidden_hook(d_hidden)`` returned (it runs between the
+    d_hidden and d_weight GEMMs, so a cross-shard reduction can overlap the d_weight GEMM), or None.
 
     For each row chunk: GEMM epilogue writes the chunk's fp32 logits (and partials); the
     per-row lse / entropy of the chunk are produced by ``stats_fn(start, end, partials, T, chunk)``
@@ -285,7 +295,7 @@ def fwd_bwd_shard(
         if done[buf] is not None:
             main.wait_event(done[buf])
         ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
-                         logits=logits)
+                         logits=logits, bias=bias)
         stats_fn(start, end, partials, T, chunk)
 
         def run_dlogits(logits=logits, start=start, end=end, rows=rows):
@@ -319,10 +329,15 @@ def fwd_bwd_shard(
     pending = dhidden_hook(d_hidden) if dhidden_hook is not None else None
     d_weight = torch.empty(V, H, device=dev, dtype=weight.dtype)
     ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
-    return d_hidden, d_weight, pending
+    d_bias = None
+    if bias is not None:
+        d_bias32 = torch.empty(V, device=dev, dtype=torch.float32)
+        ops.column_sums(dz, d_bias32, rows=B, cols=V)
+        d_bias = d_bias32.to(bias.dtype)
+    return d_hidden, d_weight, d_bias, pending
 
 
-def _megakernel_fwd_bwd(hidden_2d, weight, target_1d, chunk_size, ce_weight, ent_weight, ignore_index):
+def _megakernel_fwd_bwd(hidden_2d, weight, target_1d, chunk_size, ce_weight, ent_weight, ignore_index, bias=None):
     B = hidden_2d.shape[0]
     V = weight.shape[0]
     dev = hidden_2d.device
@@ -330,7 +345,8 @@ def _megakernel_fwd_bwd(hidden_2d, weight, target_1d, chunk_size, ce_weight, ent
     ent = torch.empty(B, device=dev, dtype=torch.float32)
     lse = torch.empty(B, device=dev, dtype=torch.float32)
     if B == 0:
-        return ce, ent, torch.zeros_like(hidden_2d), torch.zeros_like(weight)
+        return ce, ent, torch.zeros_like(hidden_2d), torch.zeros_like(weight), \
+            None if bias is None else torch.zeros_like(bias)
 
     def local_stats(start, end, partials, T, chunk):
         ops.finalize(
@@ -338,19 +354,19 @@ def _megakernel_fwd_bwd(hidden_2d, weight, target_1d, chunk_size, ce_weight, ent
             ce=ce[start:end], entropy=ent[start:end], lse=lse[start:end],
         )
 
-    d_hidden, d_weight, _ = fwd_bwd_shard(
+    d_hidden, d_weight, d_bias, _ = fwd_bwd_shard(
         hidden_2d, weight, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
-        ignore_index=ignore_index, stats_fn=local_stats,
+        ignore_index=ignore_index, stats_fn=local_stats, bias=bias,
     )
-    return ce, ent, d_hidden, d_weight
+    return ce, ent, d_hidden, d_weight, d_bias
 
 
-def _scale_grads(d_hidden: Tensor, d_weight: Tensor, dloss: Tensor):
+def _scale_grads(dloss: Tensor, *grads):
     # loss.backward() without an explicit gradient passes exactly 1.0: return the stored
     # gradients without another full pass over them.
     if dloss.numel() == 1 and float(dloss) == 1.0:
-        return d_hidden, d_weight
-    return d_hidden * dloss, d_weight * dloss
+        return grads
+    return tuple(None if g is None else g * dloss for g in grads)
 
 
 class GemmMegakernel(torch.autograd.Function):
@@ -359,12 +375,12 @@ class GemmMegakernel(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, hidden_states, weight, target, bias, chunk_size, ce_weight, ent_weight):
-        batch_shape, hidden_2d, weight_c, target_1d = _prepare(hidden_states, weight, target, bias)
-        ce, ent, d_hidden, d_weight = _megakernel_fwd_bwd(
-            hidden_2d, weight_c, target_1d, chunk_size, float(ce_weight), float(ent_weight), IGNORE_INDEX,
+        batch_shape, hidden_2d, weight_c, target_1d, bias_c = _prepare(hidden_states, weight, target, bias)
+        ce, ent, d_hidden, d_weight, d_bias = _megakernel_fwd_bwd(
+            hidden_2d, weight_c, target_1d, chunk_size, float(ce_weight), float(ent_weight), IGNORE_INDEX, bias_c,
         )
         loss = ce_weight * ce.sum() + ent_weight * ent.sum()
-        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight)
+        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight, d_bias)
         ce = ce.view(batch_shape)
         ent = ent.view(batch_shape)
         ctx.mark_non_differentiable(ce, ent)
@@ -372,9 +388,8 @@ class GemmMegakernel(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dloss, _g_ce, _g_ent):
-        d_hidden, d_weight = ctx.saved_tensors
-        d_hidden, d_weight = _scale_grads(d_hidden, d_weight, dloss)
-        return d_hidden, d_weight, None, None, None, None, None
+        d_hidden, d_weight, d_bias = _scale_grads(dloss, *ctx.saved_tensors)
+        return d_hidden, d_weight, None, d_bias, None, None, None
 
 
 def gemm_megakernel_fast(

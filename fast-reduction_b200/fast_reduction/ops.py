@@ -75,9 +75,10 @@ def fwd_partials(
     tile_stride: int,
     vocab_offset: int = 0,
     logits: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
 ) -> None:
-    """partials[t, r] <- (m, s, u, zt) of z = hidden @ weight.T over vocab tile t (see include/frx.h)."""
-    dev = _require_cuda(hidden, weight, target, partials, logits)
+    """partials[t, r] <- (m, s, u, zt) of z = hidden @ weight.T (+ bias) over vocab tile t (see include/frx.h)."""
+    dev = _require_cuda(hidden, weight, target, partials, logits, bias)
     ldh = _row_major(hidden, "hidden")
     ldw = _row_major(weight, "weight")
     rows, hdim = hidden.shape
@@ -92,6 +93,8 @@ def fwd_partials(
         raise ValueError("partials must be contiguous float32")
     if partials.numel() < 4 * n_vocab_tiles(vshard) * tile_stride:
         raise ValueError("partials buffer too small")
+    if bias is not None and (bias.dtype != torch.bfloat16 or not bias.is_contiguous() or bias.numel() != vshard):
+        raise ValueError("bias must be a contiguous bfloat16 tensor with one value per vocabulary row of the shard")
     ldl = 0
     if logits is not None:
         ldl = _row_major(logits, "logits")
@@ -99,7 +102,8 @@ def fwd_partials(
             raise ValueError("logits must be float32 [rows, >= vocab_shard]")
     lib = nat.load()
     rc = _launch("fwd_partials", dev, lambda: lib.frx_fwd_partials(
-        hidden.data_ptr(), ldh, weight.data_ptr(), ldw, nat.ptr(target), rows, vshard, hdim, vocab_offset,
+        hidden.data_ptr(), ldh, weight.data_ptr(), ldw, nat.ptr(bias), nat.ptr(target), rows, vshard, hdim,
+        vocab_offset,
         partials.data_ptr(), tile_stride, nat.ptr(logits), ldl, nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_fwd_partials")
@@ -257,3 +261,17 @@ def logits_partials(logits: torch.Tensor, target: torch.Tensor | None, partials:
         partials.data_ptr(), tile_stride, nat.stream_of(dev),
     ))
     nat.check(rc, "frx_logits_partials")
+
+
+def column_sums(x: torch.Tensor, out: torch.Tensor, *, rows: int, cols: int) -> None:
+    """out[c] <- sum_r x[r, c] for a bf16 [rows, >= cols] matrix, fp32 out (deterministic order)."""
+    dev = _require_cuda(x, out)
+    ld = _row_major(x, "x")
+    if x.dtype != torch.bfloat16:
+        raise TypeError("column_sums input must be bfloat16")
+    if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < cols:
+        raise ValueError("out must be contiguous float32 with >= cols elements")
+    lib = nat.load()
+    rc = _launch("column_sums", dev, lambda: lib.frx_column_sums(x.data_ptr(), ld, rows, cols, out.data_ptr(),
+                                                                 nat.stream_of(dev)))
+    nat.check(rc, "frx_column_sums")

@@ -63,15 +63,18 @@ def vocab_parallel_ce_entropy(
     group=None,
     chunk_size: int = 4096,
     ignore_index: int = gk.IGNORE_INDEX,
+    bias_shard: Optional[Tensor] = None,
 ) -> Tuple[Tensor, Tensor, Tensor]:
     """Forward over this rank's vocabulary slice; returns the full (ce_loss, entropy, log_probs)
-    (identical on every rank), shaped like hidden_states.shape[:-1]."""
-    batch_shape, hidden_2d, weight_shard, target_1d = gk._prepare(hidden_states, weight_shard, target, None)
+    (identical on every rank), shaped like hidden_states.shape[:-1]. ``bias_shard`` is the bias of
+    this rank's vocabulary rows, if any."""
+    batch_shape, hidden_2d, weight_shard, target_1d, bias_shard = gk._prepare(hidden_states, weight_shard, target,
+                                                                              bias_shard)
     B = hidden_2d.shape[0]
     dev = hidden_2d.device
     local = torch.empty(B, 4, device=dev, dtype=torch.float32)
     gk.forward_stats(hidden_2d, weight_shard, target_1d, chunk_size, vocab_offset=vocab_start, merged=local,
-                     vocab_size=vocab_size, ignore_index=ignore_index)
+                     vocab_size=vocab_size, ignore_index=ignore_index, bias=bias_shard)
     gathered = _gather_stats(local, group)
     ce = torch.empty(B, device=dev, dtype=torch.float32)
     ent = torch.empty(B, device=dev, dtype=torch.float32)
@@ -81,7 +84,7 @@ def vocab_parallel_ce_entropy(
 
 
 def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, vocab_size, group, chunk_size,
-                            ce_weight, ent_weight, ignore_index):
+                            ce_weight, ent_weight, ignore_index, bias_shard=None):
     B, H = hidden_2d.shape
     dev = hidden_2d.device
     ce = torch.empty(B, device=dev, dtype=torch.float32)
@@ -99,13 +102,13 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
 
     if Vr == 0:
         raise ValueError("every rank needs a non-empty vocabulary slice")
-    d_hidden_f32, d_weight, pending = gk.fwd_bwd_shard(
+    d_hidden_f32, d_weight, d_bias, pending = gk.fwd_bwd_shard(
         hidden_2d, weight_shard, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
         vocab_offset=vocab_start, ignore_index=ignore_index, stats_fn=exchange_stats, dhidden_fp32=True,
-        dhidden_hook=lambda dh: _allreduce_async(dh, group),
+        dhidden_hook=lambda dh: _allreduce_async(dh, group), bias=bias_shard,
     )
     pending.wait_into_current()
-    return ce, ent, d_hidden_f32.to(hidden_2d.dtype), d_weight
+    return ce, ent, d_hidden_f32.to(hidden_2d.dtype), d_weight, d_bias
 
 
 class _PendingAllReduce:
@@ -140,14 +143,15 @@ def _allreduce_async(t: Tensor, group) -> _PendingAllReduce:
 class VocabParallelMegakernel(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden_states, weight_shard, target, vocab_start, vocab_size, group, chunk_size, ce_weight,
-                ent_weight):
-        batch_shape, hidden_2d, weight_c, target_1d = gk._prepare(hidden_states, weight_shard, target, None)
-        ce, ent, d_hidden, d_weight = _fwd_bwd_vocab_parallel(
+                ent_weight, bias_shard):
+        batch_shape, hidden_2d, weight_c, target_1d, bias_c = gk._prepare(hidden_states, weight_shard, target,
+                                                                          bias_shard)
+        ce, ent, d_hidden, d_weight, d_bias = _fwd_bwd_vocab_parallel(
             hidden_2d, weight_c, target_1d, vocab_start, vocab_size, group, chunk_size, float(ce_weight),
-            float(ent_weight), gk.IGNORE_INDEX,
+            float(ent_weight), gk.IGNORE_INDEX, bias_c,
         )
         loss = ce_weight * ce.sum() + ent_weight * ent.sum()
-        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight)
+        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight, d_bias)
         ce = ce.view(batch_shape)
         ent = ent.view(batch_shape)
         ctx.mark_non_differentiable(ce, ent)
@@ -155,9 +159,8 @@ class VocabParallelMegakernel(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dloss, _g_ce, _g_ent):
-        d_hidden, d_weight = ctx.saved_tensors
-        d_hidden, d_weight = gk._scale_grads(d_hidden, d_weight, dloss)
-        return d_hidden, d_weight, None, None, None, None, None, None, None
+        d_hidden, d_weight, d_bias = gk._scale_grads(dloss, *ctx.saved_tensors)
+        return d_hidden, d_weight, None, None, None, None, None, None, None, d_bias
 
 
 def vocab_parallel_megakernel(
@@ -170,9 +173,10 @@ def vocab_parallel_megakernel(
     chunk_size: int = 4096,
     ce_weight: float = 1.0,
     ent_weight: float = -1.0,
+    bias_shard: Optional[Tensor] = None,
 ) -> Tuple[Tensor, Tensor, Tensor]:
     """Vocabulary-parallel gemm_megakernel_fast. Returns (loss, ce_loss, entropy), identical on
-    every rank; loss.backward() gives every rank the full d_hidden and its own weight-slice
-    gradient."""
+    every rank; loss.backward() gives every rank the full d_hidden and its own weight-slice (and
+    bias-slice) gradient."""
     return VocabParallelMegakernel.apply(hidden_states, weight_shard, target, vocab_start, vocab_size, group,
-                                         chunk_size, ce_weight, ent_weight)
+                                         chunk_size, ce_weight, ent_weight, bias_shard)

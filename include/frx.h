@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define FRX_ABI_VERSION 1
+#define FRX_ABI_VERSION 2
 
 #define FRX_OK 0
 #define FRX_ERR_INVALID_ARG 1
@@ -78,12 +78,14 @@ FRX_API const char* frx_last_error(void);
  *   z[r, j]  = sum_k hidden[r, k] * weight[j, k]        (bf16 x bf16 -> fp32, TMEM)
  *   hidden   [rows, hidden_dim] bf16, row stride ld_hidden
  *   weight   [vocab_shard, hidden_dim] bf16, row stride ld_weight (the shard's rows)
+ *   bias     optional [vocab_shard] bf16 added to every logit of its column (z = x W^T + b, as the
+ *            reference's fp32 baseline computes; the reference's own GEMM path ignores bias)
  *   target   [rows] int64 global ids, or NULL (then zt = 0)
  *   partials [ceil(vocab_shard / 256) * tile_stride] x float4, tile_stride >= rows
  *   logits   optional fp32 [rows, ld_logits] output of every z (NULL: logits never leave the chip)
  */
 FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
-                     const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
+                     const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
                      int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
                      int64_t ld_logits, int* status, void* stream);
 
@@ -135,6 +137,13 @@ FRX_API int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void
 FRX_API int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
                      void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
                      int64_t hidden_dim, int64_t rows, int* status, void* stream);
+
+/*
+ * Column sums out[c] = sum_r x[r, c] (fp32 accumulation, fixed order, so deterministic) of a bf16
+ * matrix [rows, cols] with row stride ld: the bias gradient from the dlogits of one shard.
+ * Replaces the reference's `d_bias.add_(dlogits.sum(dim=0))` (fast_reduction/gemm_kernel.py:867-869).
+ */
+FRX_API int frx_column_sums(const void* x, int64_t ld, int64_t rows, int64_t cols, float* out, void* stream);
 
 /*
  * Softmax partials of a materialised logits matrix [rows, cols] (dtype FRX_DTYPE_BF16, _F16 or

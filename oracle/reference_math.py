@@ -31,7 +31,7 @@ VOCAB_TILE = 256
 # fp32 ground truth
 # ---------------------------------------------------------------------------------------------
 def fp32_reference(hidden: torch.Tensor, weight: torch.Tensor, target: torch.Tensor,
-                   ignore_index: int = IGNORE_INDEX):
+                   ignore_index: int = IGNORE_INDEX, bias: Optional[torch.Tensor] = None):
     """fp32 matmul + fp32 reductions -> (ce, entropy, log_probs, lse), per row.
 
     Restates tests/test_ce_impls.py:17-25 (`_fp32_reference`) plus the row logsumexp. Rows whose
@@ -40,7 +40,7 @@ def fp32_reference(hidden: torch.Tensor, weight: torch.Tensor, target: torch.Ten
     h = hidden.detach().float().reshape(-1, hidden.shape[-1])
     w = weight.detach().float()
     t = target.reshape(-1)
-    logits = F.linear(h, w)
+    logits = F.linear(h, w, None if bias is None else bias.detach().float())
     lse = torch.logsumexp(logits, dim=-1)
     log_sm = logits - lse[:, None]
     sm = log_sm.exp()
@@ -73,6 +73,25 @@ def fp32_reference_grads(hidden: torch.Tensor, weight: torch.Tensor, target: tor
     ge = -torch.ones_like(ent) if g_ent is None else g_ent.reshape(-1).float().to(ent.device)
     (gc * ce + ge * ent).sum().backward()
     return ce.detach(), ent.detach(), h.grad.detach(), w.grad.detach()
+
+
+def fp32_reference_grads_with_bias(hidden: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor,
+                                   target: torch.Tensor, g_ce: Optional[torch.Tensor] = None,
+                                   g_ent: Optional[torch.Tensor] = None, ignore_index: int = IGNORE_INDEX):
+    """fp32 autograd with a bias (baseline.py:115-142: logits = F.linear(h, w, b)) ->
+    (ce, ent, d_hidden, d_weight, d_bias)."""
+    h = hidden.detach().float().reshape(-1, hidden.shape[-1]).requires_grad_(True)
+    w = weight.detach().float().requires_grad_(True)
+    b = bias.detach().float().requires_grad_(True)
+    t = target.reshape(-1)
+    log_sm = F.log_softmax(F.linear(h, w, b), dim=-1)
+    sm = log_sm.exp()
+    ce = F.nll_loss(log_sm, t, reduction="none", ignore_index=ignore_index)
+    ent = -(sm * log_sm).sum(dim=-1)
+    gc = torch.ones_like(ce) if g_ce is None else g_ce.reshape(-1).float().to(ce.device)
+    ge = -torch.ones_like(ent) if g_ent is None else g_ent.reshape(-1).float().to(ent.device)
+    (gc * ce + ge * ent).sum().backward()
+    return ce.detach(), ent.detach(), h.grad.detach(), w.grad.detach(), b.grad.detach()
 
 
 def fp32_reference_grads_chunked(hidden, weight, target, ce_weight=1.0, ent_weight=-1.0, chunk=2048,

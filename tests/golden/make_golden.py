@@ -82,6 +82,17 @@ def main() -> None:
                bwd_ent=ent.numpy(), bwd_dh=dh.numpy(), bwd_dw=dw.numpy(), bwd_gce=gce.numpy(),
                bwd_gent=gent.numpy(), bwd_dh_g=dh2.numpy(), bwd_dw_g=dw2.numpy())
 
+    # 3b. the same with a bias (baseline.py:115-142 adds it to the logits and returns d_bias).
+    torch.manual_seed(321)
+    B, H, V = 20, 32, 300
+    h = torch.randn(B, H)
+    w = torch.randn(V, H) * 0.2
+    b = torch.randn(V) * 0.5
+    t = torch.randint(0, V, (B,))
+    ce, ent, dh, dw, db = ref.baseline_linear_xent_entropy_backward(h, w, t, bias=b)
+    out.update(bias_hidden=h.numpy(), bias_weight=w.numpy(), bias_bias=b.numpy(), bias_target=t.numpy(),
+               bias_ce=ce.numpy(), bias_ent=ent.numpy(), bias_dh=dh.numpy(), bias_dw=dw.numpy(), bias_db=db.numpy())
+
     # 4. BASELINE configs[0] (B=1024, H=1024, V=32000, chunk 512, seed 0): inputs are regenerated
     #    from the seed at test time (checked by digest); only the reference's outputs are stored.
     g = torch.Generator().manual_seed(0)

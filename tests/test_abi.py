@@ -20,7 +20,7 @@ def declared_functions() -> list[str]:
 def test_header_declares_entry_points():
     names = declared_functions()
     for must in ("frx_fwd_partials", "frx_finalize", "frx_dlogits", "frx_gemm_dhidden", "frx_gemm_dweight",
-                 "frx_last_error", "frx_abi_version"):
+                 "frx_logits_partials", "frx_column_sums", "frx_last_error", "frx_abi_version"):
         assert must in names
 
 
@@ -48,7 +48,8 @@ def test_constants_match_header():
 
     hdr = HEADER.read_text()
     for name in ("FRX_OK", "FRX_ERR_INVALID_ARG", "FRX_ERR_UNSUPPORTED", "FRX_ERR_CUDA", "FRX_DTYPE_BF16",
-                 "FRX_DTYPE_F32", "FRX_VOCAB_TILE", "FRX_PARTIALS_REF_LAYOUT", "FRX_STATUS_BAD_TARGET",
+                 "FRX_DTYPE_F32", "FRX_DTYPE_F16", "FRX_VOCAB_TILE", "FRX_PARTIALS_REF_LAYOUT",
+                 "FRX_IGNORE_NEGATIVE_TARGETS", "FRX_STATUS_BAD_TARGET",
                  "FRX_STATUS_TIMEOUT_PRODUCER", "FRX_STATUS_TIMEOUT_MMA", "FRX_STATUS_TIMEOUT_EPILOGUE",
                  "FRX_STATUS_DRAIN_TIMEOUT"):
         val = int(re.search(rf"#define {name} (\d+)", hdr).group(1))
@@ -60,10 +61,10 @@ def test_invalid_arguments_return_codes_without_gpu():
 
     lib = nat.load()
     # negative sizes are rejected before any CUDA call
-    rc = lib.frx_fwd_partials(None, 0, None, 0, None, -1, 10, 64, 0, None, 0, None, 0, None, None)
+    rc = lib.frx_fwd_partials(None, 0, None, 0, None, None, -1, 10, 64, 0, None, 0, None, 0, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG
     assert b"bad sizes" in lib.frx_last_error()
-    rc = lib.frx_fwd_partials(1 << 20, 64, 1 << 21, 64, None, 8, 10, 60, 0, 1 << 22, 8, None, 0, None, None)
+    rc = lib.frx_fwd_partials(1 << 20, 64, 1 << 21, 64, None, None, 8, 10, 60, 0, 1 << 22, 8, None, 0, None, None)
     assert rc == nat.FRX_ERR_UNSUPPORTED  # hidden_dim not a multiple of 8
     rc = lib.frx_finalize(None, 3, 10, 5, 0, None, 0, 0, None, None, None, None, None, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG  # tile_stride < rows
@@ -81,5 +82,5 @@ def test_empty_problems_are_noops():
     from fast_reduction import _native as nat
 
     lib = nat.load()
-    assert lib.frx_fwd_partials(None, 0, None, 0, None, 0, 10, 64, 0, None, 0, None, 0, None, None) == nat.FRX_OK
+    assert lib.frx_fwd_partials(None, 0, None, 0, None, None, 0, 10, 64, 0, None, 0, None, 0, None, None) == nat.FRX_OK
     assert lib.frx_finalize(None, 0, 0, 0, 0, None, 0, 0, None, None, None, None, None, None, None) == nat.FRX_OK

@@ -215,3 +215,19 @@ def test_large_shape_mae_gates():
     ce32, ent32, lp32, _ = rm.fp32_reference(h, w, t)
     assert (ce - ce32).abs().mean() <= 2e-3
     assert (ent - ent32).abs().mean() <= 1e-4
+
+
+def test_forward_with_bias_matches_fp32():
+    """Bias added to every logit (the reference's fp32 baseline semantics, baseline.py:76)."""
+    from fast_reduction.gemm_kernel import gemm_fused_ce_entropy
+
+    B, H, V = 300, 256, 2000
+    h, w, t = rm.make_inputs(B, H, V, seed=31, weight_std=0.1, ignore_frac=0.05)
+    b = (torch.randn(V, generator=torch.Generator().manual_seed(2)) * 2).to(torch.bfloat16)
+    ce, ent, lp = gemm_fused_ce_entropy(h.to(DEV), w.to(DEV), t.to(DEV), bias=b.to(DEV), chunk_size=128)
+    ce_r, ent_r, lp_r, _ = rm.fp32_reference(h, w, t, bias=b)
+    torch.testing.assert_close(ce.cpu(), ce_r, atol=2e-3, rtol=1e-3)
+    torch.testing.assert_close(ent.cpu(), ent_r, atol=2e-3, rtol=1e-3)
+    # the bias really moved the result
+    ce0, _, _ = gemm_fused_ce_entropy(h.to(DEV), w.to(DEV), t.to(DEV), chunk_size=128)
+    assert (ce0.cpu() - ce_r).abs().mean() > 0.1

@@ -22,9 +22,11 @@ def test_cpu_tensors_rejected_no_fallback():
         gk.gemm_megakernel_fast(h, w, t)
 
 
-def test_bias_not_supported():
+def test_bias_checks():
     h, w, t = _inputs()
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="bias must be"):
+        gk.gemm_fused_ce_entropy(h, w, t, bias=torch.zeros(39, dtype=torch.bfloat16))
+    with pytest.raises(NotImplementedError, match="bf16"):
         gk.gemm_fused_ce_entropy(h, w, t, bias=torch.zeros(40))
 
 

@@ -142,3 +142,13 @@ def test_make_inputs_distributions():
     assert h.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and t.dtype == torch.int64
     assert abs(float(w.float().std()) - 0.05) < 0.005
     assert int((t == -100).sum()) == round(0.05 * 64)
+
+
+def test_bias_restatement_matches_reference_autograd():
+    g = GOLDEN
+    h, w, b, t = (torch.from_numpy(g[k]) for k in ("bias_hidden", "bias_weight", "bias_bias", "bias_target"))
+    ce, ent, dh, dw, db = rm.fp32_reference_grads_with_bias(h, w, b, t)
+    for got, key in ((ce, "bias_ce"), (ent, "bias_ent"), (dh, "bias_dh"), (dw, "bias_dw"), (db, "bias_db")):
+        np.testing.assert_allclose(got.numpy(), g[key], rtol=1e-5, atol=1e-6)
+    ce2, ent2, _, _ = rm.fp32_reference(h, w, t, bias=b)
+    np.testing.assert_allclose(ce2.numpy(), g["bias_ce"], rtol=1e-5, atol=1e-6)
