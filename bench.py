@@ -255,7 +255,7 @@ def run_reference(args, world, rank):
     t0 = time.perf_counter()
     rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
     probe = time.perf_counter() - t0
-    rows = int(max(64, min(2048, 64 * 3.0 / max(probe, 1e-3)))) // 64 * 64
+    rows = int(max(64, min(4096, 64 * 3.0 / max(probe, 1e-3)))) // 64 * 64
     h = torch.randn(rows, H, generator=g).to(torch.bfloat16)
     t = torch.randint(0, V, (rows,), generator=g)
     for _ in range(args.warmup):

@@ -40,22 +40,28 @@ def _worker(rank, world, port, q):
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
         B, H, V, chunk = 520, 256, 3001, 200
         h, w, t = rm.make_inputs(B, H, V, seed=5, weight_std=0.1, ignore_frac=0.05, tail_frac=0.02)
+        bias = (torch.randn(V, generator=torch.Generator().manual_seed(9)) * 0.5).to(torch.bfloat16)
         a, b = shard_bounds(V, world, rank)
         hd, td = h.to(dev), t.to(dev)
-        ce, ent, lp = vocab_parallel_ce_entropy(hd, w[a:b].to(dev), td, a, V, chunk_size=chunk)
-        ce1, ent1, lp1 = gemm_fused_ce_entropy(hd, w.to(dev), td, chunk_size=chunk)
+        ce, ent, lp = vocab_parallel_ce_entropy(hd, w[a:b].to(dev), td, a, V, chunk_size=chunk,
+                                                bias_shard=bias[a:b].to(dev))
+        ce1, ent1, lp1 = gemm_fused_ce_entropy(hd, w.to(dev), td, bias=bias.to(dev), chunk_size=chunk)
         err_fwd = max(float((ce - ce1).abs().max()), float((ent - ent1).abs().max()), float((lp - lp1).abs().max()))
 
         h_leaf = h.to(dev).requires_grad_(True)
         w_leaf = w[a:b].to(dev).requires_grad_(True)
-        loss, ce2, ent2 = vocab_parallel_megakernel(h_leaf, w_leaf, td, a, V, chunk_size=chunk)
+        b_leaf = bias[a:b].to(dev).requires_grad_(True)
+        loss, ce2, ent2 = vocab_parallel_megakernel(h_leaf, w_leaf, td, a, V, chunk_size=chunk, bias_shard=b_leaf)
         loss.backward()
         h1 = h.to(dev).requires_grad_(True)
         w1 = w.to(dev).requires_grad_(True)
-        loss1, _, _ = gemm_megakernel_fast(h1, w1, td, chunk_size=chunk)
+        b1 = bias.to(dev).requires_grad_(True)
+        loss1, _, _ = gemm_megakernel_fast(h1, w1, td, bias=b1, chunk_size=chunk)
         loss1.backward()
         dh_rel = float((h_leaf.grad.float() - h1.grad.float()).norm() / h1.grad.float().norm())
         dw_rel = float((w_leaf.grad.float() - w1.grad[a:b].float()).norm() / w1.grad[a:b].float().norm())
+        db_rel = float((b_leaf.grad.float() - b1.grad[a:b].float()).norm() / b1.grad[a:b].float().norm())
+        dw_rel = max(dw_rel, db_rel)
         loss_err = abs(float(loss) - float(loss1))
         torch.cuda.synchronize()
         bits = nat.read_status(dev)
