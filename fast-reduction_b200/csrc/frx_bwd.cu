@@ -81,6 +81,74 @@ struct StoreEpilogue {
   __device__ __forceinline__ static void finish(const Params&, int) {}
 };
 
+// Adds the fp32 accumulator tile into a multicast (NVLS) view of an fp32 matrix that every rank
+// of the vocabulary-parallel group holds: the NVSwitch sums all ranks' contributions into every
+// copy, so the d_hidden all-reduce happens inside this GEMM, tile by tile, while it computes.
+struct MultimemAddEpilogue {
+  // Two 32 x 32 fp32 staging blocks per epilogue warp: rows are re-read row-contiguously so each
+  // warp-wide reduction covers four full 128-byte row segments instead of 32 scattered 16-byte ones.
+  static constexpr int kSmemPerWarp = 2 * 32 * 32 * 4;
+  static constexpr int kSmemBytes = 4 * kSmemPerWarp;
+
+  struct Params {
+    float* mc_out;  // multicast address of the fp32 [rows, cols] accumulation buffer
+    int64_t ld_out;
+    int rows;
+    int cols;
+  };
+
+  template <class Release>
+  __device__ __forceinline__ static void run(const Params& p, uint8_t* stage, uint32_t tacc, int m_blk, int n_blk,
+                                             int q, int lane, Release release) {
+    const int row0 = m_blk * kBM + q * 32;
+    const int n0 = n_blk * kBN;
+    const int ncols = min(kBN, p.cols - n0);
+    const uint32_t stage_base = smem_u32(stage);
+    float v[32];
+#pragma unroll 1
+    for (int c = 0; c < kBN / 32; ++c) {
+      const int lim = ncols - c * 32;
+      if (lim <= 0) break;
+      __syncwarp();
+      tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
+      // lane = row: write the row's 8 16-byte chunks XOR-swizzled by row % 8 (bank-conflict free)
+      const uint32_t buf = stage_base + static_cast<uint32_t>((c & 1) * 4096);
+      const uint32_t rowb = buf + static_cast<uint32_t>(lane * 128);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        st_shared_v4(rowb + static_cast<uint32_t>((j ^ (lane & 7)) << 4), v[4 * j], v[4 * j + 1], v[4 * j + 2],
+                     v[4 * j + 3]);
+      __syncwarp();
+      // read back: lane = (row-in-group, chunk); 8 lanes cover one row's 128 bytes
+      const int j = lane & 7;
+      const int col = c * 32 + 4 * j;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = 4 * i + (lane >> 3);
+        const int row = row0 + r;
+        float4 x;
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                     : "r"(buf + static_cast<uint32_t>(r * 128 + ((j ^ (r & 7)) << 4))));
+        if (row < p.rows) {
+          float* dst = p.mc_out + static_cast<int64_t>(row) * p.ld_out + n0 + col;
+          if (col + 4 <= ncols) {
+            multimem_red_add_v4(dst, x.x, x.y, x.z, x.w);
+          } else {
+            if (col + 0 < ncols) multimem_red_add(dst + 0, x.x);
+            if (col + 1 < ncols) multimem_red_add(dst + 1, x.y);
+            if (col + 2 < ncols) multimem_red_add(dst + 2, x.z);
+          }
+        }
+      }
+    }
+    release();
+  }
+
+  // Order this thread's reductions before anything that follows the kernel at system scope.
+  __device__ __forceinline__ static void finish(const Params&, int) { __threadfence_system(); }
+};
+
 static int check_out(void* out, int64_t ld, int64_t cols, int out_dtype, const char* who) {
   FRX_REQUIRE(out != nullptr, FRX_ERR_INVALID_ARG, "%s: null output pointer", who);
   FRX_REQUIRE(out_dtype == FRX_DTYPE_BF16 || out_dtype == FRX_DTYPE_F32, FRX_ERR_INVALID_ARG,
@@ -140,4 +208,30 @@ extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const v
   return launch_gemm<true, true, true, StoreEpilogue>(a, b, vocab_shard, hidden_dim, rows, 8,
                                                 store_params(d_weight, ld_d_weight, vocab_shard, hidden_dim, out_dtype),
                                                 status, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogits, const void* weight,
+                                          int64_t ld_weight, void* d_hidden_mc, int64_t ld_d_hidden, int64_t rows,
+                                          int64_t hidden_dim, int64_t vocab_shard, int* status, void* stream) {
+  using namespace frx;
+  FRX_REQUIRE(rows >= 0 && hidden_dim >= 1 && vocab_shard >= 1 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
+                  vocab_shard < (1ll << 31),
+              FRX_ERR_INVALID_ARG, "frx_gemm_dhidden_multicast: bad sizes");
+  if (rows == 0) return FRX_OK;
+  FRX_REQUIRE(dlogits != nullptr && weight != nullptr && d_hidden_mc != nullptr, FRX_ERR_INVALID_ARG,
+              "frx_gemm_dhidden_multicast: null pointer");
+  FRX_REQUIRE(ld_d_hidden >= hidden_dim, FRX_ERR_INVALID_ARG, "frx_gemm_dhidden_multicast: ld_d_hidden < hidden_dim");
+  MultimemAddEpilogue::Params ep;
+  ep.mc_out = static_cast<float*>(d_hidden_mc);
+  ep.ld_out = ld_d_hidden;
+  ep.rows = static_cast<int>(rows);
+  ep.cols = static_cast<int>(hidden_dim);
+  FRX_REQUIRE(aligned16(d_hidden_mc) && ld_d_hidden % 4 == 0, FRX_ERR_INVALID_ARG,
+              "frx_gemm_dhidden_multicast: the multicast buffer must be 16-byte aligned with ld a multiple of 4");
+  Operand a{dlogits, ld_dlogits, rows, vocab_shard, false};
+  Operand b{weight, ld_weight, hidden_dim, vocab_shard, true};
+  // 256 x 256 tiles with the double-buffered TMEM accumulator: each tile's NVLink reductions run
+  // while the next tile's MMAs do, instead of stalling a single-buffered 256 x 512 tile.
+  return launch_gemm<false, true, false, MultimemAddEpilogue>(a, b, rows, hidden_dim, vocab_shard, 8, ep, status,
+                                                              static_cast<cudaStream_t>(stream));
 }

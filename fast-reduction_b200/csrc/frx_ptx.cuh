@@ -331,6 +331,20 @@ __device__ __forceinline__ void umma_commit_pair_mc(uint64_t* bar, uint16_t cta_
 }
 
 // ---------------------------------------------------------------------------------------
+// NVLink SHARP (NVLS) multicast reductions
+// ---------------------------------------------------------------------------------------
+// Adds four fp32 values into the same address of every GPU bound to the multicast object that
+// `mc` points into; the NVSwitch performs the reduction.
+__device__ __forceinline__ void multimem_red_add_v4(float* mc, float a, float b, float c, float d) {
+  asm volatile("multimem.red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ void multimem_red_add(float* mc, float a) {
+  asm volatile("multimem.red.relaxed.sys.global.add.f32 [%0], %1;" ::"l"(mc), "f"(a) : "memory");
+}
+
+// ---------------------------------------------------------------------------------------
 // misc math
 // ---------------------------------------------------------------------------------------
 // Hardware base-2 exponential (MUFU.EX2), flush-to-zero; |rel err| ~ 2^-22.

@@ -254,14 +254,16 @@ def fwd_bwd_shard(
     stats_fn=None,
     g_ce: Optional[Tensor] = None,
     g_ent: Optional[Tensor] = None,
-    dhidden_fp32: bool = False,
-    dhidden_hook=None,
+    dhidden_fn=None,
     bias: Optional[Tensor] = None,
 ):
-    """Training pass over one vocabulary shard; returns (d_hidden [B, H], d_weight [V_shard, H],
-    d_bias [V_shard] or None, pending) where d_hidden is this shard's contribution (fp32 if
-    ``dhidden_fp32``) and ``pending`` is what ``dhidden_hook(d_hidden)`` returned (it runs between the
-    d_hidden and d_weight GEMMs, so a cross-shard reduction can overlap the d_weight GEMM), or None.
+    """Training pass over one vocabulary shard; returns (d_hidden, d_weight [V_shard, H],
+    d_bias [V_shard] or None, pending).
+
+    By default d_hidden is this shard's [B, H] contribution in the hidden dtype and pending is None.
+    A ``dhidden_fn(dz)`` replaces that step (it runs between the dlogits pass and the d_weight GEMM,
+    so a cross-shard reduction it starts overlaps the d_weight GEMM) and its (d_hidden, pending) pair
+    is returned instead.
 
     For each row chunk: GEMM epilogue writes the chunk's fp32 logits (and partials); the
     per-row lse / entropy of the chunk are produced by ``stats_fn(start, end, partials, T, chunk)``
@@ -324,9 +326,12 @@ def fwd_bwd_shard(
             if t_ is not None:
                 t_.record_stream(side)
     del logits_bufs, partials
-    d_hidden = torch.empty(B, H, device=dev, dtype=torch.float32 if dhidden_fp32 else hidden_2d.dtype)
-    ops.gemm_dhidden(dz, weight, d_hidden, rows=B, vocab_shard=V)
-    pending = dhidden_hook(d_hidden) if dhidden_hook is not None else None
+    if dhidden_fn is not None:
+        d_hidden, pending = dhidden_fn(dz)
+    else:
+        d_hidden = torch.empty(B, H, device=dev, dtype=hidden_2d.dtype)
+        ops.gemm_dhidden(dz, weight, d_hidden, rows=B, vocab_shard=V)
+        pending = None
     d_weight = torch.empty(V, H, device=dev, dtype=weight.dtype)
     ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
     d_bias = None

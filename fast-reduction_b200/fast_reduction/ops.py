@@ -275,3 +275,23 @@ def column_sums(x: torch.Tensor, out: torch.Tensor, *, rows: int, cols: int) -> 
     rc = _launch("column_sums", dev, lambda: lib.frx_column_sums(x.data_ptr(), ld, rows, cols, out.data_ptr(),
                                                                  nat.stream_of(dev)))
     nat.check(rc, "frx_column_sums")
+
+
+def gemm_dhidden_multicast(dz: torch.Tensor, weight: torch.Tensor, mc_ptr: int, ld_out: int, *, rows: int,
+                           vocab_shard: int, device: torch.device) -> None:
+    """Adds dz[rows, vocab_shard] @ weight[vocab_shard, H] into the fp32 matrix behind the NVLS
+    multicast address `mc_ptr` (row stride ld_out): the cross-rank d_hidden sum inside the GEMM."""
+    dev = _require_cuda(dz, weight)
+    if dz.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("dz and weight must be bfloat16")
+    if not mc_ptr:
+        raise ValueError("a multicast address is required")
+    ldz = _row_major(dz, "dz")
+    ldw = _row_major(weight, "weight")
+    hdim = weight.shape[1]
+    lib = nat.load()
+    rc = _launch("gemm_dhidden", dev, lambda: lib.frx_gemm_dhidden_multicast(
+        dz.data_ptr(), ldz, weight.data_ptr(), ldw, mc_ptr, ld_out, rows, hdim, vocab_shard,
+        nat.status_word(dev).data_ptr(), nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_gemm_dhidden_multicast")

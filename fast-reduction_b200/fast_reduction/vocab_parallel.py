@@ -8,15 +8,20 @@ rank) and merges them with the same associative rule as the per-tile merge
 (reference merge: fast_reduction/gemm_ce_entropy_finalize.py:78-92). Every rank then holds the
 full ce / entropy / lse.
 
-Training: dlogits and d_weight of a slice are local; d_hidden is a sum over slices, so each rank
-computes its partial d_hidden in fp32 and one all-reduce (on a side stream, overlapped with the
-d_weight GEMM) completes it.
+Training: dlogits and d_weight of a slice are local; d_hidden is a sum over slices. Each rank
+computes its partial d_hidden in fp32 and one NCCL all-reduce on a side stream, overlapped with the
+d_weight GEMM, completes it. An alternative (FRX_NVLS=1) fuses the sum into the d_hidden GEMM: its
+epilogue adds every finished fp32 tile into all ranks' copies of a symmetric-memory buffer through
+the NVSwitch (`frx_gemm_dhidden_multicast`, multimem.red). It is correct but slower on B200 at this
+volume (512 MiB of reductions per rank: the fused GEMM took 13.5 ms vs 11.5 ms + overlapped NCCL at
+2 GPUs, 6.8 ms vs 2.8 ms at 8 GPUs), so NCCL is the default.
 
 The reference is single-GPU; this module adds the sharded path around the same libfrx kernels.
 """
 
 from __future__ import annotations
 
+import os
 from typing import Optional, Tuple
 
 import torch
@@ -25,6 +30,33 @@ from torch import Tensor
 
 from . import gemm_kernel as gk
 from . import ops
+
+
+# FRX_NVLS=1 selects the multicast-fused d_hidden reduction (when the GPUs support NVLS).
+_USE_NVLS = os.environ.get("FRX_NVLS", "0") == "1"
+_nvls_buffers: dict = {}
+
+
+def _nvls_dhidden_buffer(rows: int, hidden: int, device: torch.device, group):
+    """Symmetric-memory fp32 [rows, hidden] buffer bound to an NVLS multicast object, cached per
+    (group, shape, device), or (None, None) when multicast is unavailable. Collective: every rank
+    of the group calls it with the same shape."""
+    pg = group if group is not None else dist.group.WORLD
+    key = (id(pg), rows, hidden, device.index)
+    hit = _nvls_buffers.get(key)
+    if hit is None:
+        hit = (None, None)
+        try:
+            import torch.distributed._symmetric_memory as symm
+
+            buf = symm.empty(rows, hidden, dtype=torch.float32, device=device)
+            hdl = symm.rendezvous(buf, pg)
+            if hdl.multicast_ptr:
+                hit = (buf, hdl)
+        except Exception:
+            hit = (None, None)
+        _nvls_buffers[key] = hit
+    return hit
 
 
 def shard_bounds(vocab_size: int, world_size: int, rank: int) -> Tuple[int, int]:
@@ -102,11 +134,31 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
 
     if Vr == 0:
         raise ValueError("every rank needs a non-empty vocabulary slice")
+    buf, hdl = (None, None)
+    if _USE_NVLS and dist.get_world_size(group) > 1:
+        buf, hdl = _nvls_dhidden_buffer(B, H, dev, group)
+    if buf is not None:
+        # Zeroed before the forward chunks: their all-gathers order every rank's zeroing before any
+        # rank's d_hidden GEMM starts adding into the buffers.
+        buf.zero_()
+
+        def dhidden_fn(dz):
+            ops.gemm_dhidden_multicast(dz, weight_shard, hdl.multicast_ptr, H, rows=B, vocab_shard=Vr, device=dev)
+            return None, None
+    else:
+        def dhidden_fn(dz):
+            dh = torch.empty(B, H, device=dev, dtype=torch.float32)
+            ops.gemm_dhidden(dz, weight_shard, dh, rows=B, vocab_shard=Vr)
+            return dh, _allreduce_async(dh, group)
+
     d_hidden_f32, d_weight, d_bias, pending = gk.fwd_bwd_shard(
         hidden_2d, weight_shard, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
-        vocab_offset=vocab_start, ignore_index=ignore_index, stats_fn=exchange_stats, dhidden_fp32=True,
-        dhidden_hook=lambda dh: _allreduce_async(dh, group), bias=bias_shard,
+        vocab_offset=vocab_start, ignore_index=ignore_index, stats_fn=exchange_stats, dhidden_fn=dhidden_fn,
+        bias=bias_shard,
     )
+    if buf is not None:
+        hdl.barrier()  # every rank's reductions have landed in every copy
+        return ce, ent, buf.to(hidden_2d.dtype), d_weight, d_bias
     pending.wait_into_current()
     return ce, ent, d_hidden_f32.to(hidden_2d.dtype), d_weight, d_bias
 

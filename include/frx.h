@@ -129,6 +129,20 @@ FRX_API int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void
                      int64_t vocab_shard, int* status, void* stream);
 
 /*
+ * Vocabulary-parallel d_hidden with the cross-rank sum fused into the GEMM: this rank's
+ * contribution dlogits[rows, vocab_shard] @ weight[vocab_shard, hidden_dim] is ADDED, tile by tile
+ * from the epilogue, into an fp32 [rows, hidden_dim] matrix through its NVLink-SHARP multicast
+ * address `d_hidden_mc` (multimem.red.add), so every rank's copy ends up holding the sum over ranks.
+ * The caller zeroes every rank's copy before any rank calls this, and synchronises the ranks after
+ * all of them have called it before reading. Replaces the GEMM + separate NCCL all-reduce of
+ * d_hidden (no counterpart in the single-GPU reference; its d_hidden GEMM is
+ * fast_reduction/gemm_kernel.py:859-862).
+ */
+FRX_API int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogits, const void* weight,
+                                       int64_t ld_weight, void* d_hidden_mc, int64_t ld_d_hidden, int64_t rows,
+                                       int64_t hidden_dim, int64_t vocab_shard, int* status, void* stream);
+
+/*
  * d_weight[vocab_shard, hidden_dim] = dlogits[rows, vocab_shard]^T @ hidden[rows, hidden_dim]
  * accumulated over all `rows` in fp32 tensor memory and written once in out_dtype. Replaces
  * the per-chunk `d_weight.add_(torch.mm(dlogits.t(), h_chunk).float())` and the final cast

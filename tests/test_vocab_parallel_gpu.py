@@ -17,12 +17,14 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, nvls):
     try:
         import datetime
+        import os
         import sys
         from pathlib import Path
 
+        os.environ["FRX_NVLS"] = "1" if nvls else "0"  # read when fast_reduction.vocab_parallel is imported
         repo = Path(__file__).resolve().parents[1]
         for p in (str(repo / "fast-reduction_b200"), str(repo)):
             if p not in sys.path:
@@ -73,12 +75,15 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least two GPUs")
-def test_vocab_parallel_matches_single_gpu():
+@pytest.mark.parametrize("nvls", [True, False], ids=["nvls-fused-dhidden", "nccl-allreduce"])
+def test_vocab_parallel_matches_single_gpu(nvls):
+    """Both d_hidden reductions: the NCCL all-reduce (default) and the reduction fused into the GEMM
+    through NVLS multicast (FRX_NVLS=1; when the GPUs lack NVLS this case runs the NCCL path too)."""
     world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, nvls)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
