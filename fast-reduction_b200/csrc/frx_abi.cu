@@ -81,9 +81,10 @@ static int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes
   return FRX_OK;
 }
 
-int encode_bf16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
-                   int box_cols) {
-  return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols, ld, box_rows, box_cols);
+int encode_16bit_2d(CUtensorMap* map, bool f16, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows, int box_cols) {
+  return encode_2d(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, rows, cols,
+                   ld, box_rows, box_cols);
 }
 
 int encode_f32_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,

@@ -6,11 +6,26 @@
 // Both read their operands in place (no transposed copies): the MN-major operands are
 // fetched as 64 x 64 TMA boxes and described to tcgen05.mma with the MN-major bit. d_weight
 // is accumulated over the whole batch in fp32 tensor memory and written once.
+#include <cstring>
+
 #include "frx_host.cuh"
 
 namespace frx {
 
-// Writes the fp32 accumulator tile as bf16 or fp32 rows: each thread owns one output row and
+// Packs two floats into a bf16x2 or fp16x2 word (round to nearest even), low half first.
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
+  uint32_t w;
+  if (f16) {
+    const __half2 h = __floats2half2_rn(a, b);
+    memcpy(&w, &h, sizeof(w));
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    memcpy(&w, &h, sizeof(w));
+  }
+  return w;
+}
+
+// Writes the fp32 accumulator tile as bf16, fp16 or fp32 rows: each thread owns one output row and
 // stores 32 consecutive columns per TMEM load.
 struct StoreEpilogue {
   static constexpr int kSmemPerWarp = 0;
@@ -22,7 +37,8 @@ struct StoreEpilogue {
     int rows;
     int cols;
     int out_f32;
-    int vec_ok;  // base and ld allow 16-byte vector stores
+    int out_f16;  // 16-bit output is fp16 (else bf16)
+    int vec_ok;   // base and ld allow 16-byte vector stores
   };
 
   template <class Release>
@@ -53,25 +69,22 @@ struct StoreEpilogue {
             if (j < lim) dst[j] = v[j];
         }
       } else {
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + off;
+        const bool f16 = p.out_f16 != 0;
+        uint16_t* dst = static_cast<uint16_t*>(p.out) + off;
         if (lim >= 32 && p.vec_ok) {
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             uint4 pk;
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[j], v[j + 1]);
-            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[j + 2], v[j + 3]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[j + 4], v[j + 5]);
-            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[j + 6], v[j + 7]);
-            pk.x = *reinterpret_cast<uint32_t*>(&h0);
-            pk.y = *reinterpret_cast<uint32_t*>(&h1);
-            pk.z = *reinterpret_cast<uint32_t*>(&h2);
-            pk.w = *reinterpret_cast<uint32_t*>(&h3);
+            pk.x = pack2(v[j], v[j + 1], f16);
+            pk.y = pack2(v[j + 2], v[j + 3], f16);
+            pk.z = pack2(v[j + 4], v[j + 5], f16);
+            pk.w = pack2(v[j + 6], v[j + 7], f16);
             *reinterpret_cast<uint4*>(dst + j) = pk;
           }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (j < lim) dst[j] = __float2bfloat16_rn(v[j]);
+            if (j < lim) dst[j] = static_cast<uint16_t>(pack2(v[j], 0.0f, f16) & 0xFFFFu);
         }
       }
     }
@@ -151,8 +164,8 @@ struct MultimemAddEpilogue {
 
 static int check_out(void* out, int64_t ld, int64_t cols, int out_dtype, const char* who) {
   FRX_REQUIRE(out != nullptr, FRX_ERR_INVALID_ARG, "%s: null output pointer", who);
-  FRX_REQUIRE(out_dtype == FRX_DTYPE_BF16 || out_dtype == FRX_DTYPE_F32, FRX_ERR_INVALID_ARG,
-              "%s: out_dtype must be FRX_DTYPE_BF16 or FRX_DTYPE_F32", who);
+  FRX_REQUIRE(out_dtype == FRX_DTYPE_BF16 || out_dtype == FRX_DTYPE_F16 || out_dtype == FRX_DTYPE_F32,
+              FRX_ERR_INVALID_ARG, "%s: out_dtype must be FRX_DTYPE_BF16, FRX_DTYPE_F16 or FRX_DTYPE_F32", who);
   FRX_REQUIRE(ld >= cols, FRX_ERR_INVALID_ARG, "%s: output leading dimension %lld < %lld columns", who,
               (long long)ld, (long long)cols);
   return FRX_OK;
@@ -165,6 +178,7 @@ static StoreEpilogue::Params store_params(void* out, int64_t ld, int64_t rows, i
   ep.rows = static_cast<int>(rows);
   ep.cols = static_cast<int>(cols);
   ep.out_f32 = out_dtype == FRX_DTYPE_F32 ? 1 : 0;
+  ep.out_f16 = out_dtype == FRX_DTYPE_F16 ? 1 : 0;
   const int64_t elem = ep.out_f32 ? 4 : 2;
   ep.vec_ok = aligned16(out) && ((ld * elem) % 16 == 0) ? 1 : 0;
   return ep;
@@ -173,7 +187,7 @@ static StoreEpilogue::Params store_params(void* out, int64_t ld, int64_t rows, i
 }  // namespace frx
 
 extern "C" int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void* weight, int64_t ld_weight,
-                                void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows, int64_t hidden_dim,
+                                int in_dtype, void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows, int64_t hidden_dim,
                                 int64_t vocab_shard, int* status, void* stream) {
   using namespace frx;
   FRX_REQUIRE(rows >= 0 && hidden_dim >= 1 && vocab_shard >= 1 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
@@ -184,15 +198,15 @@ extern "C" int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const v
   FRX_REQUIRE(dlogits != nullptr && weight != nullptr, FRX_ERR_INVALID_ARG, "frx_gemm_dhidden: null input pointer");
   int rc = check_out(d_hidden, ld_d_hidden, hidden_dim, out_dtype, "frx_gemm_dhidden");
   if (rc) return rc;
-  Operand a{dlogits, ld_dlogits, rows, vocab_shard, false};  // [rows, V] row-major, K = V contiguous
-  Operand b{weight, ld_weight, hidden_dim, vocab_shard, true};  // [V, H] row-major, N = H contiguous
+  Operand a{dlogits, ld_dlogits, rows, vocab_shard, false, in_dtype};  // [rows, V] row-major, K = V contiguous
+  Operand b{weight, ld_weight, hidden_dim, vocab_shard, true, in_dtype};  // [V, H] row-major, N = H contiguous
   return launch_gemm<false, true, true, StoreEpilogue>(a, b, rows, hidden_dim, vocab_shard, 8,
                                                  store_params(d_hidden, ld_d_hidden, rows, hidden_dim, out_dtype),
                                                  status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
-                                void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
+                                int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
                                 int64_t hidden_dim, int64_t rows, int* status, void* stream) {
   using namespace frx;
   FRX_REQUIRE(rows >= 1 && hidden_dim >= 1 && vocab_shard >= 0 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
@@ -203,16 +217,17 @@ extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const v
   FRX_REQUIRE(dlogits != nullptr && hidden != nullptr, FRX_ERR_INVALID_ARG, "frx_gemm_dweight: null input pointer");
   int rc = check_out(d_weight, ld_d_weight, hidden_dim, out_dtype, "frx_gemm_dweight");
   if (rc) return rc;
-  Operand a{dlogits, ld_dlogits, vocab_shard, rows, true};  // [rows, V] row-major, M = V contiguous
-  Operand b{hidden, ld_hidden, hidden_dim, rows, true};     // [rows, H] row-major, N = H contiguous
+  Operand a{dlogits, ld_dlogits, vocab_shard, rows, true, in_dtype};  // [rows, V] row-major, M = V contiguous
+  Operand b{hidden, ld_hidden, hidden_dim, rows, true, in_dtype};     // [rows, H] row-major, N = H contiguous
   return launch_gemm<true, true, true, StoreEpilogue>(a, b, vocab_shard, hidden_dim, rows, 8,
                                                 store_params(d_weight, ld_d_weight, vocab_shard, hidden_dim, out_dtype),
                                                 status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogits, const void* weight,
-                                          int64_t ld_weight, void* d_hidden_mc, int64_t ld_d_hidden, int64_t rows,
-                                          int64_t hidden_dim, int64_t vocab_shard, int* status, void* stream) {
+                                          int64_t ld_weight, int in_dtype, void* d_hidden_mc, int64_t ld_d_hidden,
+                                          int64_t rows, int64_t hidden_dim, int64_t vocab_shard, int* status,
+                                          void* stream) {
   using namespace frx;
   FRX_REQUIRE(rows >= 0 && hidden_dim >= 1 && vocab_shard >= 1 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
                   vocab_shard < (1ll << 31),
@@ -228,8 +243,8 @@ extern "C" int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogit
   ep.cols = static_cast<int>(hidden_dim);
   FRX_REQUIRE(aligned16(d_hidden_mc) && ld_d_hidden % 4 == 0, FRX_ERR_INVALID_ARG,
               "frx_gemm_dhidden_multicast: the multicast buffer must be 16-byte aligned with ld a multiple of 4");
-  Operand a{dlogits, ld_dlogits, rows, vocab_shard, false};
-  Operand b{weight, ld_weight, hidden_dim, vocab_shard, true};
+  Operand a{dlogits, ld_dlogits, rows, vocab_shard, false, in_dtype};
+  Operand b{weight, ld_weight, hidden_dim, vocab_shard, true, in_dtype};
   // 256 x 256 tiles with the double-buffered TMEM accumulator: each tile's NVLink reductions run
   // while the next tile's MMAs do, instead of stalling a single-buffered 256 x 512 tile.
   return launch_gemm<false, true, false, MultimemAddEpilogue>(a, b, rows, hidden_dim, vocab_shard, 8, ep, status,

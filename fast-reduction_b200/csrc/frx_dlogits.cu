@@ -4,9 +4,9 @@
 //   dz_j = p_j * (g_ce - g_ent * (log p_j + H)) - g_ce * [j == target]
 //
 // (reference: fast_reduction/cute_dlogits.py:87-100). Pure streaming kernel, HBM-bound:
-// reads fp32 logits once, writes bf16 (or fp32) dlogits once. Each thread handles 16
+// reads fp32 logits once, writes bf16 (or fp16 / fp32) dlogits once. Each thread handles 16
 // consecutive columns of a row (four 16-byte streaming loads issued back to back, two 16-byte
-// bf16 stores); the per-row constants A = g_ce - g_ent * H and B = -g_ent are formed once per
+// 16-bit stores); the per-row constants A = g_ce - g_ent * H and B = -g_ent are formed once per
 // thread, after the loads are in flight.
 #include "frx_host.cuh"
 
@@ -22,7 +22,11 @@ __device__ __forceinline__ float dz_value(float z, float row_lse, float a, float
   return p * fmaf(b, lp, a);
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+__device__ __forceinline__ uint32_t pack_16x2(float lo, float hi, bool f16) {
+  if (f16) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
@@ -31,7 +35,7 @@ __global__ void __launch_bounds__(kDlThreads)
     dlogits_kernel(const float* __restrict__ logits, int64_t ld_logits, const int64_t* __restrict__ target,
                    const float* __restrict__ lse, const float* __restrict__ ent, const float* __restrict__ g_ce,
                    const float* __restrict__ g_ent, float ce_weight, float ent_weight, void* __restrict__ out,
-                   int64_t ld_out, int out_f32, int64_t rows, int64_t cols, int64_t vocab_offset,
+                   int64_t ld_out, int out_f32, int out_f16, int64_t rows, int64_t cols, int64_t vocab_offset,
                    int64_t ignore_index, int vec_ok) {
   const int64_t c0 = (static_cast<int64_t>(blockIdx.x) * kDlThreads + threadIdx.x) * kDlVec;
   if (c0 >= cols) return;
@@ -85,21 +89,22 @@ __global__ void __launch_bounds__(kDlThreads)
           if (c0 + i < cols) orow[c0 + i] = d[i];
       }
     } else {
-      __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(out) + row * ld_out;
+      const bool f16 = out_f16 != 0;
+      uint16_t* orow = static_cast<uint16_t*>(out) + row * ld_out;
       if (full) {
 #pragma unroll
         for (int i = 0; i < kDlVec; i += 8) {
           uint4 pk;
-          pk.x = pack_bf16x2(d[i], d[i + 1]);
-          pk.y = pack_bf16x2(d[i + 2], d[i + 3]);
-          pk.z = pack_bf16x2(d[i + 4], d[i + 5]);
-          pk.w = pack_bf16x2(d[i + 6], d[i + 7]);
+          pk.x = pack_16x2(d[i], d[i + 1], f16);
+          pk.y = pack_16x2(d[i + 2], d[i + 3], f16);
+          pk.z = pack_16x2(d[i + 4], d[i + 5], f16);
+          pk.w = pack_16x2(d[i + 6], d[i + 7], f16);
           __stcs(reinterpret_cast<uint4*>(orow + c0 + i), pk);
         }
       } else {
 #pragma unroll
         for (int i = 0; i < kDlVec; ++i)
-          if (c0 + i < cols) orow[c0 + i] = __float2bfloat16_rn(d[i]);
+          if (c0 + i < cols) orow[c0 + i] = static_cast<uint16_t>(pack_16x2(d[i], 0.0f, f16) & 0xFFFFu);
       }
     }
   }
@@ -116,11 +121,12 @@ extern "C" int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t
   if (rows == 0 || vocab_shard == 0) return FRX_OK;
   FRX_REQUIRE(logits != nullptr && lse != nullptr && entropy != nullptr && dlogits != nullptr, FRX_ERR_INVALID_ARG,
               "frx_dlogits: null logits/lse/entropy/dlogits pointer");
-  FRX_REQUIRE(out_dtype == FRX_DTYPE_BF16 || out_dtype == FRX_DTYPE_F32, FRX_ERR_INVALID_ARG,
-              "frx_dlogits: out_dtype must be FRX_DTYPE_BF16 or FRX_DTYPE_F32");
+  FRX_REQUIRE(out_dtype == FRX_DTYPE_BF16 || out_dtype == FRX_DTYPE_F16 || out_dtype == FRX_DTYPE_F32,
+              FRX_ERR_INVALID_ARG, "frx_dlogits: out_dtype must be FRX_DTYPE_BF16, FRX_DTYPE_F16 or FRX_DTYPE_F32");
   FRX_REQUIRE(ld_logits >= vocab_shard && ld_dlogits >= vocab_shard, FRX_ERR_INVALID_ARG,
               "frx_dlogits: leading dimensions must be >= vocab_shard");
   const int out_f32 = out_dtype == FRX_DTYPE_F32 ? 1 : 0;
+  const int out_f16 = out_dtype == FRX_DTYPE_F16 ? 1 : 0;
   const int64_t out_elem = out_f32 ? 4 : 2;
   const int vec_ok = aligned16(logits) && aligned16(dlogits) && (ld_logits % 4 == 0) &&
                      ((ld_dlogits * out_elem) % 16 == 0);
@@ -130,7 +136,7 @@ extern "C" int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t
   dim3 grid(static_cast<unsigned>(gx), gy);
   dlogits_kernel<<<grid, kDlThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       logits, ld_logits, target, lse, entropy, g_ce, g_ent, ce_weight, ent_weight, dlogits, ld_dlogits, out_f32,
-      rows, vocab_shard, vocab_offset, ignore_index, vec_ok);
+      out_f16, rows, vocab_shard, vocab_offset, ignore_index, vec_ok);
   FRX_CUDA_CHECK(cudaGetLastError());
   return FRX_OK;
 }

@@ -9,7 +9,8 @@
 // The reference computes the same four numbers per (row, 256-column tile) in
 // fast_reduction/gemm_ce_entropy_epilogue.py:184-271 (its third slot is sum z exp(z - m)).
 // Columns at or beyond the shard's vocabulary size are skipped, not sentinel-filled. An optional
-// bf16 bias is added to each column before the reductions (and before the logits store).
+// bias (bf16 or fp16, the operands' type) is added to each column before the reductions (and
+// before the logits store).
 #include <cstring>
 
 #include "frx_host.cuh"
@@ -31,8 +32,18 @@ __device__ __forceinline__ float select32(const float (&v)[32], int idx) {
   return (idx & 1) ? w2[1] : w2[0];
 }
 
-// v[j] += bias[j] for the valid columns of a 32-column chunk (bf16 bias, fp32 add).
-__device__ __forceinline__ void add_bias32(float (&v)[32], const __nv_bfloat16* b, int lim, bool vec) {
+// The two 16-bit values packed in `w` (low half first) as floats: bf16 or fp16.
+__device__ __forceinline__ float2 unpack2(uint32_t w, bool f16) {
+  if (f16) {
+    __half2 h;
+    memcpy(&h, &w, sizeof(h));
+    return __half22float2(h);
+  }
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+
+// v[j] += bias[j] for the valid columns of a 32-column chunk (16-bit bias, fp32 add).
+__device__ __forceinline__ void add_bias32(float (&v)[32], const uint16_t* b, int lim, bool vec, bool f16) {
   if (lim >= 32 && vec) {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -40,14 +51,15 @@ __device__ __forceinline__ void add_bias32(float (&v)[32], const __nv_bfloat16* 
       const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        v[8 * q + 2 * i] += __uint_as_float(u[i] << 16);
-        v[8 * q + 2 * i + 1] += __uint_as_float(u[i] & 0xFFFF0000u);
+        const float2 f = unpack2(u[i], f16);
+        v[8 * q + 2 * i] += f.x;
+        v[8 * q + 2 * i + 1] += f.y;
       }
     }
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      if (j < lim) v[j] += __bfloat162float(b[j]);
+      if (j < lim) v[j] += unpack2(b[j], f16).x;
   }
 }
 
@@ -59,7 +71,7 @@ struct CEPartialsEpilogue {
   struct Params {
     CUtensorMap tm_logits;  // fp32 [rows, vocab_shard] logits, 32 x 32 boxes, 128B swizzle
     const int64_t* target;
-    const __nv_bfloat16* bias;  // optional [vocab_shard] bias of this shard
+    const uint16_t* bias;  // optional [vocab_shard] bias of this shard (bf16 or fp16 bits)
     int64_t vocab_offset;
     int rows;
     int vocab_shard;
@@ -67,6 +79,7 @@ struct CEPartialsEpilogue {
     int64_t tile_stride;
     int has_logits;
     int bias_vec;  // bias base 16-byte aligned
+    int f16;       // bias is fp16 (else bf16)
   };
 
   template <class Release>
@@ -93,7 +106,7 @@ struct CEPartialsEpilogue {
       if (lim <= 0) break;
       __syncwarp();  // tcgen05.ld is warp-collective: reconverge after per-row branches
       tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
-      if (p.bias != nullptr) add_bias32(v, p.bias + n0 + c * 32, lim, p.bias_vec != 0);
+      if (p.bias != nullptr) add_bias32(v, p.bias + n0 + c * 32, lim, p.bias_vec != 0, p.f16 != 0);
       if (lim >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
@@ -135,7 +148,7 @@ struct CEPartialsEpilogue {
       if (lim <= 0) break;
       __syncwarp();
       tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
-      if (p.bias != nullptr) add_bias32(v, p.bias + n0 + c * 32, lim, p.bias_vec != 0);
+      if (p.bias != nullptr) add_bias32(v, p.bias + n0 + c * 32, lim, p.bias_vec != 0, p.f16 != 0);
       if (lim >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
@@ -171,7 +184,7 @@ struct CEPartialsEpilogue {
 }  // namespace frx
 
 extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
-                                const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
+                                int dtype, const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
                                 int64_t hidden_dim,
                                 int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
                                 int64_t ld_logits, int* status, void* stream) {
@@ -186,6 +199,8 @@ extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const voi
               "frx_fwd_partials: null hidden/weight/partials pointer");
   FRX_REQUIRE(hidden_dim % 8 == 0, FRX_ERR_UNSUPPORTED, "frx_fwd_partials: hidden_dim %lld must be a multiple of 8",
               (long long)hidden_dim);
+  FRX_REQUIRE(is_gemm_dtype(dtype), FRX_ERR_UNSUPPORTED,
+              "frx_fwd_partials: dtype %d must be FRX_DTYPE_BF16 or FRX_DTYPE_F16", dtype);
   FRX_REQUIRE(tile_stride >= rows, FRX_ERR_INVALID_ARG, "frx_fwd_partials: tile_stride %lld < rows %lld",
               (long long)tile_stride, (long long)rows);
   FRX_REQUIRE((reinterpret_cast<uintptr_t>(partials) & 15u) == 0, FRX_ERR_INVALID_ARG,
@@ -203,15 +218,16 @@ extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const voi
     ep.has_logits = 1;
   }
   ep.target = target;
-  ep.bias = static_cast<const __nv_bfloat16*>(bias);
+  ep.bias = static_cast<const uint16_t*>(bias);
   ep.bias_vec = aligned16(bias) ? 1 : 0;
+  ep.f16 = dtype == FRX_DTYPE_F16 ? 1 : 0;
   ep.vocab_offset = vocab_offset;
   ep.rows = static_cast<int>(rows);
   ep.vocab_shard = static_cast<int>(vocab_shard);
   ep.partials = reinterpret_cast<float4*>(partials);
   ep.tile_stride = tile_stride;
-  Operand a{hidden, ld_hidden, rows, hidden_dim, false};
-  Operand b{weight, ld_weight, vocab_shard, hidden_dim, false};
+  Operand a{hidden, ld_hidden, rows, hidden_dim, false, dtype};
+  Operand b{weight, ld_weight, vocab_shard, hidden_dim, false, dtype};
   // A band of up to 64 row blocks (8192 rows, 64 MiB of bf16 hidden at H=4096) stays in L2
   // while the CTAs sweep the vocabulary.
   return launch_gemm<false, false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, 64, ep, status,

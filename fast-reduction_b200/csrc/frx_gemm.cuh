@@ -48,6 +48,7 @@ struct TileSched {
   int group;
   int num_tiles;
   int n256;  // number of 256-column blocks of the output (epilogue bound for wide tiles)
+  int f16;   // operands are fp16 (else bf16)
   __device__ __forceinline__ void get(int t, int& m_blk, int& n_blk) const {
     const int per_band = group * num_n;
     const int band = t / per_band;
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(kBM, kBN, kAMN, kBMN);
+      const uint32_t idesc = make_idesc_f32acc(kBM, kBN, kAMN, kBMN, sched.f16 != 0);
       constexpr uint32_t a_lbo = kAMN ? kMNBoxBytes : 16;
       constexpr uint32_t b_lbo = kBMN ? kMNBoxBytes : 16;
       constexpr uint32_t a_kstep = kAMN ? 16 * 128 : 32;  // bytes per UMMA_K (=16) step
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kBK / 16; ++k) {
             const uint64_t adesc = make_smem_desc_sw128(a_addr + k * a_kstep, a_lbo, 1024);
             const uint64_t bdesc = make_smem_desc_sw128(b_addr + k * b_kstep, b_lbo, 1024);
-            umma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[stage]);  // frees this smem slot once the MMAs have read it
           if (++stage == kStages) {
@@ -394,7 +395,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (even CTA)
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = make_idesc_bf16_f32(2 * kBM, 256, kAMN, kBMN);
+      const uint32_t idesc = make_idesc_f32acc(2 * kBM, 256, kAMN, kBMN, sched.f16 != 0);
       constexpr uint32_t a_lbo = kAMN ? kMNBoxBytes : 16;
       constexpr uint32_t b_lbo = kBMN ? kMNBoxBytes : 16;
       constexpr uint32_t a_kstep = kAMN ? 16 * 128 : 32;  // bytes per UMMA_K (= 16) step
@@ -431,7 +432,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
               for (int h = 0; h < kNH; ++h) {
                 const uint64_t bdesc =
                     make_smem_desc_sw128(b_addr + (ks * kNH + h) * kPairSubBytes + k * b_kstep, b_lbo, 1024);
-                umma_bf16_pair(d_tmem + static_cast<uint32_t>(h * 256), adesc, bdesc, idesc, acc);
+                umma_f16_pair(d_tmem + static_cast<uint32_t>(h * 256), adesc, bdesc, idesc, acc);
               }
             }
           }

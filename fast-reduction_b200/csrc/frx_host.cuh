@@ -41,11 +41,11 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Number of SMs of the current device (cached per device ordinal).
 int sm_count(int* out);
 
-// Encodes a 2-D bf16 TMA descriptor over a row-major matrix [rows, cols] with row stride
-// `ld` elements, box [box_rows, box_cols] (box_cols * 2 bytes == 128 for the swizzle),
+// Encodes a 2-D TMA descriptor over a row-major bf16 (or fp16, `f16`) matrix [rows, cols] with row
+// stride `ld` elements, box [box_rows, box_cols] (box_cols * 2 bytes == 128 for the swizzle),
 // 128-byte swizzle, zero fill outside the matrix.
-int encode_bf16_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
-                   int box_cols);
+int encode_16bit_2d(CUtensorMap* map, bool f16, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows, int box_cols);
 
 // Same for an fp32 matrix (box_cols * 4 bytes == 128), used for TMA stores of logits tiles.
 int encode_f32_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t ld, int box_rows,
@@ -63,7 +63,7 @@ int ensure_smem_attr(Kernel kernel, std::atomic<uint64_t>& done_mask, int bytes)
   return FRX_OK;
 }
 
-// Operand descriptor for the GEMM core: a row-major bf16 matrix plus how the GEMM reads it.
+// Operand descriptor for the GEMM core: a row-major bf16 / fp16 matrix plus how the GEMM reads it.
 // K-major: the matrix is [mn_extent, k_extent]; MN-major: the matrix is [k_extent, mn_extent].
 struct Operand {
   const void* ptr;
@@ -71,11 +71,16 @@ struct Operand {
   int64_t mn_extent;
   int64_t k_extent;
   bool mn_major;
+  int dtype = FRX_DTYPE_BF16;  // FRX_DTYPE_BF16 or FRX_DTYPE_F16
 };
 
+// The 16-bit operand formats of the GEMM core.
+inline bool is_gemm_dtype(int dtype) { return dtype == FRX_DTYPE_BF16 || dtype == FRX_DTYPE_F16; }
+
 inline int encode_operand(CUtensorMap* map, const Operand& op, int tile_mn) {
-  if (op.mn_major) return encode_bf16_2d(map, op.ptr, op.k_extent, op.mn_extent, op.ld, kBK, 64);
-  return encode_bf16_2d(map, op.ptr, op.mn_extent, op.k_extent, op.ld, tile_mn, kBK);
+  const bool f16 = op.dtype == FRX_DTYPE_F16;
+  if (op.mn_major) return encode_16bit_2d(map, f16, op.ptr, op.k_extent, op.mn_extent, op.ld, kBK, 64);
+  return encode_16bit_2d(map, f16, op.ptr, op.mn_extent, op.k_extent, op.ld, tile_mn, kBK);
 }
 
 // Which GEMM core runs: the CTA-pair kernel (default) or the single-CTA kernel. The
@@ -118,6 +123,8 @@ int max_pair_clusters(Kernel kernel, std::atomic<int>* cache, int smem_bytes, in
 template <bool kAMN, bool kBMN, bool kWide, class Epi>
 int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_t K, int group_m,
                 const typename Epi::Params& ep, int* status, cudaStream_t stream) {
+  FRX_REQUIRE(is_gemm_dtype(a.dtype) && a.dtype == b.dtype, FRX_ERR_INVALID_ARG,
+              "GEMM operands must both be bf16 or both fp16 (dtype codes %d, %d)", a.dtype, b.dtype);
   const bool pair = use_pair_kernel();
   const int b_rows = pair ? 128 : kBN;
   CUtensorMap tm_a, tm_b;
@@ -132,6 +139,7 @@ int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_
   sched.num_m = static_cast<int>((M + tile_m - 1) / tile_m);
   sched.num_n = static_cast<int>((N + tile_n - 1) / tile_n);
   sched.n256 = static_cast<int>((N + 255) / 256);
+  sched.f16 = a.dtype == FRX_DTYPE_F16 ? 1 : 0;
   const int group = pair ? (group_m + 1) / 2 : group_m;
   sched.group = group < 1 ? 1 : (group > sched.num_m ? sched.num_m : group);
   const long long tiles = static_cast<long long>(sched.num_m) * sched.num_n;

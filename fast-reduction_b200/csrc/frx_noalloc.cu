@@ -73,8 +73,8 @@ extern "C" int frx_fwd_ce_entropy_noalloc(const void* hidden, int64_t ld_hidden,
   int rc = fwd_scratch_device_ptr(&scratch);
   if (rc) return rc;
   float* partials = static_cast<float*>(scratch);
-  rc = frx_fwd_partials(hidden, ld_hidden, weight, ld_weight, nullptr, target, rows, vocab_size, hidden_dim, 0,
-                        partials, rows, nullptr, 0, status, stream);
+  rc = frx_fwd_partials(hidden, ld_hidden, weight, ld_weight, FRX_DTYPE_BF16, nullptr, target, rows, vocab_size,
+                        hidden_dim, 0, partials, rows, nullptr, 0, status, stream);
   if (rc) return rc;
   return frx_finalize(partials, n_tiles, rows, rows, 0, target, vocab_size, ignore_index, ce, entropy, lse, log_probs,
                       nullptr, status, stream);

@@ -10,6 +10,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace frx {
@@ -179,8 +180,9 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, bf16 inputs, fp32 accumulator, one CTA.
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, 16-bit float inputs (kind::f16: bf16 or fp16, as the
+// instruction descriptor says), fp32 accumulator, one CTA.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                           uint32_t accumulate) {
   const uint32_t no_mask = 0u;
   asm volatile(
@@ -243,12 +245,13 @@ __device__ __forceinline__ uint64_t make_smem_desc_sw128(uint32_t saddr, uint32_
   return d;
 }
 
-// Instruction descriptor for tcgen05.mma kind::f16 with bf16 A/B and an fp32 accumulator.
-// Fields: D format (1 = f32) at [4,6), A format (1 = bf16) at [7,10), B format at [10,13),
-// A major (1 = MN-major) bit 15, B major bit 16, N >> 3 at [17,23), M >> 4 at [24,29).
-__host__ __device__ constexpr uint32_t make_idesc_bf16_f32(int m, int n, bool a_mn_major, bool b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16) |
-         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+// Instruction descriptor for tcgen05.mma kind::f16 with bf16 or fp16 A/B (both the same) and an
+// fp32 accumulator. Fields: D format (1 = f32) at [4,6), A format (0 = f16, 1 = bf16) at [7,10),
+// B format at [10,13), A major (1 = MN-major) bit 15, B major bit 16, N >> 3 at [17,23),
+// M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t make_idesc_f32acc(int m, int n, bool a_mn_major, bool b_mn_major, bool f16) {
+  return (1u << 4) | ((f16 ? 0u : 1u) << 7) | ((f16 ? 0u : 1u) << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+         ((b_mn_major ? 1u : 0u) << 16) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -302,7 +305,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 // D[tmem of both CTAs] (+)= A * B^T for an M = 256 tile split over the CTA pair (issued by
 // the even CTA; each CTA supplies its own 128 rows of A and half of B from the same smem
 // offsets).
-__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                                uint32_t accumulate) {
   const uint32_t no_mask = 0u;
   asm volatile(

@@ -192,11 +192,12 @@ extern "C" int frx_logits_partials(const void* logits, int dtype, int64_t ld, in
 
 namespace frx {
 
-// out[c] = sum over rows of x[r, c]: a CTA owns 256 columns (8 per lane, 16-byte loads); its 8
-// warps take every 8th row, four rows in flight each, and the per-warp sums are added in a fixed
-// order through shared memory.
+// out[c] = sum over rows of x[r, c] (x bf16, or fp16 when kF16): a CTA owns 256 columns (8 per
+// lane, 16-byte loads); its 8 warps take every 8th row, four rows in flight each, and the per-warp
+// sums are added in a fixed order through shared memory.
+template <bool kF16>
 __global__ void __launch_bounds__(256)
-    column_sums_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t rows, int64_t cols,
+    column_sums_kernel(const uint16_t* __restrict__ x, int64_t ld, int64_t rows, int64_t cols,
                        float* __restrict__ out, int vec_ok) {
   __shared__ float red[8][256];
   const int lane = threadIdx.x & 31;
@@ -206,19 +207,29 @@ __global__ void __launch_bounds__(256)
   if (c0 < cols) {
     const bool full = vec_ok && c0 + 8 <= cols;
     for (int64_t r = warp; r < rows; r += 8) {
-      const __nv_bfloat16* xr = x + r * ld + c0;
+      const uint16_t* xr = x + r * ld + c0;
       if (full) {
         const uint4 q = __ldcs(reinterpret_cast<const uint4*>(xr));
         const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          acc[2 * i] += __uint_as_float(w[i] << 16);
-          acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+          if (kF16) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+          } else {
+            acc[2 * i] += __uint_as_float(w[i] << 16);
+            acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+          }
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (c0 + i < cols) acc[i] += __bfloat162float(xr[i]);
+        for (int i = 0; i < 8; ++i) {
+          if (c0 + i < cols) {
+            const uint16_t b = xr[i];
+            acc[i] += kF16 ? __half2float(__ushort_as_half(b)) : __uint_as_float(static_cast<uint32_t>(b) << 16);
+          }
+        }
       }
     }
   }
@@ -236,16 +247,20 @@ __global__ void __launch_bounds__(256)
 
 }  // namespace frx
 
-extern "C" int frx_column_sums(const void* x, int64_t ld, int64_t rows, int64_t cols, float* out, void* stream) {
+extern "C" int frx_column_sums(const void* x, int dtype, int64_t ld, int64_t rows, int64_t cols, float* out,
+                               void* stream) {
   using namespace frx;
   FRX_REQUIRE(rows >= 0 && cols >= 0 && ld >= cols, FRX_ERR_INVALID_ARG, "frx_column_sums: bad sizes");
+  FRX_REQUIRE(dtype == FRX_DTYPE_BF16 || dtype == FRX_DTYPE_F16, FRX_ERR_INVALID_ARG,
+              "frx_column_sums: dtype must be FRX_DTYPE_BF16 or FRX_DTYPE_F16");
   if (cols == 0) return FRX_OK;
   FRX_REQUIRE(out != nullptr && (x != nullptr || rows == 0), FRX_ERR_INVALID_ARG, "frx_column_sums: null pointer");
   const int vec_ok = aligned16(x) && ld % 8 == 0;
   const int64_t blocks = (cols + 255) / 256;
   FRX_REQUIRE(blocks < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_column_sums: too many columns");
-  column_sums_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ld, rows, cols, out, vec_ok);
+  auto kernel = dtype == FRX_DTYPE_F16 ? column_sums_kernel<true> : column_sums_kernel<false>;
+  kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(x), ld, rows, cols, out, vec_ok);
   FRX_CUDA_CHECK(cudaGetLastError());
   return FRX_OK;
 }

@@ -51,18 +51,19 @@ _F32 = ctypes.c_float
 SIGNATURES: dict[str, tuple] = {
     "frx_abi_version": (_I32, []),
     "frx_last_error": (ctypes.c_char_p, []),
-    "frx_fwd_partials": (_I32, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P, _P]),
+    "frx_fwd_partials": (_I32, [_P, _I64, _P, _I64, _I32, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P,
+                                _P]),
     "frx_finalize": (_I32, [_P, _I64, _I64, _I64, _I32, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P]),
     "frx_dlogits": (
         _I32,
         [_P, _I64, _P, _P, _P, _P, _P, _F32, _F32, _P, _I64, _I32, _I64, _I64, _I64, _I64, _P],
     ),
-    "frx_gemm_dhidden": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
-    "frx_gemm_dweight": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
+    "frx_gemm_dhidden": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
+    "frx_gemm_dweight": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
     "frx_fwd_ce_entropy_noalloc": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
     "frx_logits_partials": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P]),
-    "frx_column_sums": (_I32, [_P, _I64, _I64, _I64, _P, _P]),
-    "frx_gemm_dhidden_multicast": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P]),
+    "frx_column_sums": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _P]),
+    "frx_gemm_dhidden_multicast": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I64, _I64, _I64, _P, _P]),
 }
 
 _lib = None

@@ -13,7 +13,7 @@ Engine (all device work is libfrx, sm_100a):
   forward   frx_fwd_partials: tcgen05 GEMM whose epilogue reduces each 128x256 fp32 TMEM tile to
             per-row softmax partials; logits never reach HBM.  frx_finalize: partials -> ce/H/lse.
   training  the same GEMM also streams fp32 logits of one row chunk to HBM; frx_dlogits turns
-            them into bf16 dlogits for all rows; frx_gemm_dhidden / frx_gemm_dweight run once
+            them into bf16 (fp16) dlogits for all rows; frx_gemm_dhidden / frx_gemm_dweight run once
             over the full batch (d_weight accumulates over every row in TMEM: no fp32 d_weight
             read-modify-write per chunk, no transposed weight copy).
 
@@ -56,10 +56,30 @@ def _side_stream(dev: torch.device) -> torch.cuda.Stream:
     return st
 
 
-def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Optional[Tensor]):
-    if hidden_states.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+def _input_device(*tensors: Optional[Tensor]) -> Optional[torch.device]:
+    """None when every given tensor is on a GPU; otherwise (some are host tensors) the device the
+    host-streamed path runs on: the CUDA device of the GPU-resident ones, else the current one."""
+    cuda = [t.device for t in tensors if t is not None and t.is_cuda]
+    host = [t for t in tensors if t is not None and t.device.type == "cpu"]
+    if not host:
+        return None
+    for t in tensors:
+        if t is not None and not t.is_cuda and t.device.type != "cpu":
+            raise ValueError(f"inputs must be CUDA or CPU tensors, got one on {t.device}")
+    if any(d != cuda[0] for d in cuda):
+        raise ValueError(f"CUDA inputs must share one device, got {sorted(set(map(str, cuda)))}")
+    if cuda:
+        return cuda[0]
+    if not torch.cuda.is_available():
+        raise RuntimeError("fast_reduction (B200 engine) needs a CUDA device; none is visible")
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Optional[Tensor], allow_host: bool = False):
+    if hidden_states.dtype != weight.dtype or hidden_states.dtype not in (torch.bfloat16, torch.float16):
         raise NotImplementedError(
-            f"the B200 engine computes in bf16; got hidden {hidden_states.dtype}, weight {weight.dtype}"
+            "the B200 engine computes in bf16 or fp16 (hidden and weight of the same type); got hidden "
+            f"{hidden_states.dtype}, weight {weight.dtype}"
         )
     if weight.dim() != 2:
         raise ValueError(f"weight must be [V, H], got shape {tuple(weight.shape)}")
@@ -85,10 +105,11 @@ def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Option
     if bias is not None:
         if bias.dim() != 1 or bias.numel() != weight.shape[0]:
             raise ValueError(f"bias must be [V={weight.shape[0]}], got shape {tuple(bias.shape)}")
-        if bias.dtype != torch.bfloat16:
-            raise NotImplementedError(f"bias must be bf16 like the weight, got {bias.dtype}")
+        if bias.dtype != weight.dtype:
+            raise NotImplementedError(f"bias must have the weight's dtype {weight.dtype}, got {bias.dtype}")
         bias = bias.contiguous()
-    ops._require_cuda(hidden_2d, weight, target_1d, bias)
+    if not (allow_host and _input_device(hidden_2d, weight, target_1d, bias) is not None):
+        ops._require_cuda(hidden_2d, weight, target_1d, bias)
     return batch_shape, hidden_2d, weight, target_1d, bias
 
 
@@ -143,6 +164,126 @@ def forward_stats(
         )
 
 
+# Host-resident inputs (forward_stats_from_host): the weight is uploaded in slices of this many
+# 256-row vocabulary tiles, so the GEMM over one slice runs while the next is in flight.
+_HOST_SLICE_TILES = 32
+# Bound on the [tiles, rows, 4] fp32 partials buffer of the host-streamed path.
+_HOST_PARTIALS_BYTES = 1 << 30
+_copy_streams: dict = {}
+
+
+def _copy_stream(dev: torch.device) -> torch.cuda.Stream:
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _copy_streams.get(idx)
+    if st is None:
+        st = torch.cuda.Stream(device=torch.device("cuda", idx))
+        _copy_streams[idx] = st
+    return st
+
+
+def _to_device(t: Optional[Tensor], dev: torch.device, stream: torch.cuda.Stream) -> Optional[Tensor]:
+    """`t` itself when it already lives on `dev`, else an upload of it enqueued on `stream`."""
+    if t is None or t.device == dev:
+        return t
+    out = torch.empty(t.shape, dtype=t.dtype, device=dev)
+    with torch.cuda.stream(stream):
+        out.copy_(t, non_blocking=True)
+    return out
+
+
+def forward_stats_from_host(
+    hidden_2d: Tensor,
+    weight: Tensor,
+    target_1d: Tensor,
+    dev: torch.device,
+    *,
+    bias: Optional[Tensor] = None,
+    vocab_offset: int = 0,
+    vocab_size: Optional[int] = None,
+    ignore_index: int = IGNORE_INDEX,
+    ce: Optional[Tensor] = None,
+    entropy: Optional[Tensor] = None,
+    lse: Optional[Tensor] = None,
+    log_probs: Optional[Tensor] = None,
+    merged: Optional[Tensor] = None,
+    hidden_share=None,
+) -> None:
+    """forward_stats when some inputs are host (CPU) tensors: the uploads overlap the GEMMs.
+
+    On a copy stream: target, bias and hidden (whichever are on the host), then the weight in slices
+    of _HOST_SLICE_TILES vocabulary tiles. The current stream launches one GEMM-epilogue per weight
+    slice over all rows of a row group as soon as that slice is resident; each launch writes the
+    partials of its own vocabulary tiles, so the result equals the device-resident path bit for bit
+    (the same tiles, each reduced in the same order). Outputs are device tensors given by the caller.
+    Host inputs should be pinned for the copies to overlap; pageable memory is correct but serialises.
+
+    ``hidden_share = (rank, world, gather)`` splits the upload of a host ``hidden_2d`` over ranks that
+    all hold the same rows: this rank uploads only rows [rank*c, (rank+1)*c) of c = ceil(B/world) into
+    a [c, H] buffer, and ``gather(share)`` (enqueued on the current stream, e.g. an NCCL all-gather)
+    returns the [world*c, H] device tensor whose first B rows are hidden.
+    """
+    B, H = hidden_2d.shape
+    V = weight.shape[0]
+    if B == 0:
+        return
+    cur = torch.cuda.current_stream(dev)
+    cp = _copy_stream(dev)
+    # Device buffers come from the current stream's pool: copies into them start after its prior work.
+    cp.wait_stream(cur)
+    share_ev = None
+    if hidden_share is not None and hidden_2d.device != dev:
+        rank, world, gather = hidden_share
+        c = (B + world - 1) // world
+        lo, hi = min(B, rank * c), min(B, (rank + 1) * c)
+        share = torch.empty(c, H, dtype=hidden_2d.dtype, device=dev)
+        with torch.cuda.stream(cp):
+            if hi > lo:
+                share[: hi - lo].copy_(hidden_2d[lo:hi], non_blocking=True)
+            share_ev = torch.cuda.Event()
+            share_ev.record(cp)
+        h_d = None
+    else:
+        h_d = _to_device(hidden_2d, dev, cp)
+    t_d = _to_device(target_1d, dev, cp)
+    b_d = _to_device(bias, dev, cp)
+    # slices: (first row, end row, event after which the slice and every earlier upload are resident)
+    slices = []
+    step = V if weight.device == dev else _HOST_SLICE_TILES * ops.VOCAB_TILE
+    w_d = weight if weight.device == dev else torch.empty(weight.shape, dtype=weight.dtype, device=dev)
+    with torch.cuda.stream(cp):
+        for a in range(0, V, step):
+            b = min(a + step, V)
+            if w_d is not weight:
+                w_d[a:b].copy_(weight[a:b], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(cp)
+            slices.append((a, b, ev))
+    if share_ev is not None:
+        cur.wait_event(share_ev)
+        h_d = gather(share)[:B]
+    T = ops.n_vocab_tiles(V)
+    group = max(ops.VOCAB_TILE, _HOST_PARTIALS_BYTES // (16 * T) // ops.VOCAB_TILE * ops.VOCAB_TILE)
+    group = min(group, B)
+    partials = torch.empty(T, group, 4, device=dev, dtype=torch.float32)
+    vocab_size = V if vocab_size is None else vocab_size
+    for start in range(0, B, group):
+        end = min(start + group, B)
+        for a, b, ev in slices:
+            if start == 0:
+                cur.wait_event(ev)
+            ops.fwd_partials(h_d[start:end], w_d[a:b], t_d[start:end], partials[a // ops.VOCAB_TILE:], group,
+                             vocab_offset + a, bias=None if b_d is None else b_d[a:b])
+        ops.finalize(
+            partials, T, end - start, group,
+            target=t_d[start:end], vocab_size=vocab_size, ignore_index=ignore_index,
+            ce=None if ce is None else ce[start:end],
+            entropy=None if entropy is None else entropy[start:end],
+            lse=None if lse is None else lse[start:end],
+            log_probs=None if log_probs is None else log_probs[start:end],
+            merged=None if merged is None else merged[start:end],
+        )
+
+
 def gemm_fused_ce_entropy(
     hidden_states: Tensor,
     weight: Tensor,
@@ -154,8 +295,21 @@ def gemm_fused_ce_entropy(
     ignore_index: int = IGNORE_INDEX,
 ) -> Tuple[Tensor, Tensor, Tensor]:
     """Fused linear + CE + entropy forward. Returns (ce_loss, entropy, log_probs), each fp32
-    and shaped like ``hidden_states.shape[:-1]``. The [chunk, V] logits never reach HBM."""
-    batch_shape, hidden_2d, weight, target_1d, bias = _prepare(hidden_states, weight, target, bias)
+    and shaped like ``hidden_states.shape[:-1]``. The [chunk, V] logits never reach HBM.
+
+    Inputs may also be host (CPU) tensors, ideally pinned: they are uploaded to the GPU of the
+    CUDA inputs (else the current device) with the weight streamed in slices under the GEMMs, and
+    the results are returned on ``hidden_states``' device (the call waits for them when that is
+    the host)."""
+    batch_shape, hidden_2d, weight, target_1d, bias = _prepare(hidden_states, weight, target, bias,
+                                                               allow_host=True)
+    dev = _input_device(hidden_2d, weight, target_1d, bias)
+    if dev is not None:
+        B = hidden_2d.shape[0]
+        ce, ent, logp = (torch.empty(B, device=dev, dtype=torch.float32) for _ in range(3))
+        forward_stats_from_host(hidden_2d, weight, target_1d, dev, bias=bias, ce=ce, entropy=ent, log_probs=logp,
+                                ignore_index=ignore_index)
+        return _results_to(hidden_states.device, batch_shape, ce, ent, logp)
     B = hidden_2d.shape[0]
     dev = hidden_2d.device
     ce = torch.empty(B, device=dev, dtype=torch.float32)
@@ -166,13 +320,27 @@ def gemm_fused_ce_entropy(
     return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
 
 
+def _results_to(out_dev: torch.device, batch_shape, *results: Tensor) -> Tuple[Tensor, ...]:
+    """Per-row results shaped like ``batch_shape`` on ``out_dev``; for the host, copied into pinned
+    buffers on the current stream and waited for."""
+    if out_dev.type != "cpu":
+        return tuple(r.to(out_dev).view(batch_shape) for r in results)
+    outs = tuple(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in results)
+    for o, r in zip(outs, results):
+        o.copy_(r, non_blocking=True)
+    done = torch.cuda.Event()
+    done.record(torch.cuda.current_stream(results[0].device))
+    done.synchronize()
+    return tuple(o.view(batch_shape) for o in outs)
+
+
 class GemmFusedCEEntropy(torch.autograd.Function):
     """Differentiable forward (reference GemmFusedCEEntropy, gemm_kernel.py:541-568).
 
     Forward: the GEMM-epilogue path (no logits in HBM); saves the per-row lse and entropy.
     Backward(g_ce, g_ent, g_lp): arbitrary per-row upstream gradients; since log_probs = -ce,
     the CE weight is g_ce - g_lp (reference :559-562). The logits are recomputed chunk by chunk by
-    the same deterministic GEMM (bitwise equal to the forward's), turned into bf16 dlogits with
+    the same deterministic GEMM (bitwise equal to the forward's), turned into 16-bit dlogits with
     the per-row weights, and fed to the d_hidden / d_weight GEMMs.
     """
 
@@ -268,7 +436,7 @@ def fwd_bwd_shard(
     For each row chunk: GEMM epilogue writes the chunk's fp32 logits (and partials); the
     per-row lse / entropy of the chunk are produced by ``stats_fn(start, end, partials, T, chunk)``
     (single GPU: a local finalize; vocabulary-parallel: local merge + cross-rank exchange);
-    frx_dlogits writes bf16 dlogits of the chunk into a [B, V_shard] buffer. Then one
+    frx_dlogits writes the chunk's dlogits (in the operands' 16-bit type) into a [B, V_shard] buffer. Then one
     d_hidden GEMM and one d_weight GEMM over all rows.
     """
     B, H = hidden_2d.shape
@@ -283,7 +451,7 @@ def fwd_bwd_shard(
     # forward GEMM of chunk c+1 (tensor-bound); the GEMM of chunk c+2 waits for it.
     logits_bufs = [torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32)
                    for _ in range(2 if overlap else 1)]
-    dz = torch.empty(B, ops.round_up(V, 8), device=dev, dtype=torch.bfloat16)
+    dz = torch.empty(B, ops.round_up(V, 8), device=dev, dtype=hidden_2d.dtype)
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev) if overlap else None
     if side is not None:

@@ -46,6 +46,19 @@ def round_up(x: int, m: int) -> int:
     return (x + m - 1) // m * m
 
 
+# Operand types of the tcgen05 GEMMs (kind::f16: both operands bf16, or both fp16).
+_GEMM_DTYPES = {torch.bfloat16: nat.FRX_DTYPE_BF16, torch.float16: nat.FRX_DTYPE_F16}
+_OUT_DTYPES = {**_GEMM_DTYPES, torch.float32: nat.FRX_DTYPE_F32}
+
+
+def _gemm_dtype(*tensors: torch.Tensor) -> int:
+    """FRX dtype code shared by the GEMM operands; raises unless all are bf16 or all fp16."""
+    dts = {t.dtype for t in tensors}
+    if len(dts) != 1 or next(iter(dts)) not in _GEMM_DTYPES:
+        raise TypeError(f"GEMM operands must all be bfloat16 or all float16, got {sorted(map(str, dts))}")
+    return _GEMM_DTYPES[next(iter(dts))]
+
+
 def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
     dev = None
     for t in tensors:
@@ -85,16 +98,16 @@ def fwd_partials(
     vshard = weight.shape[0]
     if weight.shape[1] != hdim:
         raise ValueError(f"hidden dim mismatch: hidden {tuple(hidden.shape)} vs weight {tuple(weight.shape)}")
-    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
-        raise TypeError("hidden and weight must be bfloat16")
+    dt = _gemm_dtype(hidden, weight)
     if target is not None and (target.dtype != torch.int64 or not target.is_contiguous() or target.numel() < rows):
         raise ValueError("target must be a contiguous int64 tensor with one id per row")
     if partials.dtype != torch.float32 or not partials.is_contiguous():
         raise ValueError("partials must be contiguous float32")
     if partials.numel() < 4 * n_vocab_tiles(vshard) * tile_stride:
         raise ValueError("partials buffer too small")
-    if bias is not None and (bias.dtype != torch.bfloat16 or not bias.is_contiguous() or bias.numel() != vshard):
-        raise ValueError("bias must be a contiguous bfloat16 tensor with one value per vocabulary row of the shard")
+    if bias is not None and (bias.dtype != hidden.dtype or not bias.is_contiguous() or bias.numel() != vshard):
+        raise ValueError("bias must be a contiguous tensor of the weight's dtype with one value per vocabulary row "
+                         "of the shard")
     ldl = 0
     if logits is not None:
         ldl = _row_major(logits, "logits")
@@ -102,7 +115,7 @@ def fwd_partials(
             raise ValueError("logits must be float32 [rows, >= vocab_shard]")
     lib = nat.load()
     rc = _launch("fwd_partials", dev, lambda: lib.frx_fwd_partials(
-        hidden.data_ptr(), ldh, weight.data_ptr(), ldw, nat.ptr(bias), nat.ptr(target), rows, vshard, hdim,
+        hidden.data_ptr(), ldh, weight.data_ptr(), ldw, dt, nat.ptr(bias), nat.ptr(target), rows, vshard, hdim,
         vocab_offset,
         partials.data_ptr(), tile_stride, nat.ptr(logits), ldl, nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
@@ -165,18 +178,15 @@ def dlogits(
     vocab_offset: int = 0,
     ignore_index: int = NO_IGNORE,
 ) -> None:
-    """out[r, j] <- d(sum g_ce*ce + g_ent*H)/dz[r, j] from fp32 logits (bf16 or fp32 out)."""
+    """out[r, j] <- d(sum g_ce*ce + g_ent*H)/dz[r, j] from fp32 logits (bf16, fp16 or fp32 out)."""
     dev = _require_cuda(logits, target, lse, entropy, out, g_ce, g_ent)
     ldl = _row_major(logits, "logits")
     ldo = _row_major(out, "dlogits")
     if logits.dtype != torch.float32:
         raise TypeError("logits must be float32")
-    if out.dtype == torch.bfloat16:
-        odt = nat.FRX_DTYPE_BF16
-    elif out.dtype == torch.float32:
-        odt = nat.FRX_DTYPE_F32
-    else:
-        raise TypeError("dlogits output must be bfloat16 or float32")
+    odt = _OUT_DTYPES.get(out.dtype)
+    if odt is None:
+        raise TypeError("dlogits output must be bfloat16, float16 or float32")
     if logits.shape[0] < rows or out.shape[0] < rows or logits.shape[1] < vocab_shard or out.shape[1] < vocab_shard:
         raise ValueError("logits/out smaller than [rows, vocab_shard]")
     for name, t in (("lse", lse), ("entropy", entropy), ("g_ce", g_ce), ("g_ent", g_ent)):
@@ -194,18 +204,15 @@ def dlogits(
 
 
 def _out_dtype(t: torch.Tensor) -> int:
-    if t.dtype == torch.bfloat16:
-        return nat.FRX_DTYPE_BF16
-    if t.dtype == torch.float32:
-        return nat.FRX_DTYPE_F32
-    raise TypeError("GEMM output must be bfloat16 or float32")
+    if t.dtype not in _OUT_DTYPES:
+        raise TypeError("GEMM output must be bfloat16, float16 or float32")
+    return _OUT_DTYPES[t.dtype]
 
 
 def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int) -> None:
     """out[rows, H] <- dz[rows, vocab_shard] @ weight[vocab_shard, H]."""
     dev = _require_cuda(dz, weight, out)
-    if dz.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
-        raise TypeError("dz and weight must be bfloat16")
+    dt = _gemm_dtype(dz, weight)
     ldz = _row_major(dz, "dz")
     ldw = _row_major(weight, "weight")
     ldo = _row_major(out, "d_hidden")
@@ -214,7 +221,8 @@ def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, r
         raise ValueError("shape mismatch in gemm_dhidden")
     lib = nat.load()
     rc = _launch("gemm_dhidden", dev, lambda: lib.frx_gemm_dhidden(
-        dz.data_ptr(), ldz, weight.data_ptr(), ldw, out.data_ptr(), ldo, _out_dtype(out), rows, hdim, vocab_shard,
+        dz.data_ptr(), ldz, weight.data_ptr(), ldw, dt, out.data_ptr(), ldo, _out_dtype(out), rows, hdim,
+        vocab_shard,
         nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_gemm_dhidden")
@@ -223,8 +231,7 @@ def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, r
 def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int) -> None:
     """out[vocab_shard, H] <- dz[rows, vocab_shard]^T @ hidden[rows, H]."""
     dev = _require_cuda(dz, hidden, out)
-    if dz.dtype != torch.bfloat16 or hidden.dtype != torch.bfloat16:
-        raise TypeError("dz and hidden must be bfloat16")
+    dt = _gemm_dtype(dz, hidden)
     ldz = _row_major(dz, "dz")
     ldh = _row_major(hidden, "hidden")
     ldo = _row_major(out, "d_weight")
@@ -233,7 +240,7 @@ def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, r
         raise ValueError("shape mismatch in gemm_dweight")
     lib = nat.load()
     rc = _launch("gemm_dweight", dev, lambda: lib.frx_gemm_dweight(
-        dz.data_ptr(), ldz, hidden.data_ptr(), ldh, out.data_ptr(), ldo, _out_dtype(out), vocab_shard, hdim, rows,
+        dz.data_ptr(), ldz, hidden.data_ptr(), ldh, dt, out.data_ptr(), ldo, _out_dtype(out), vocab_shard, hdim, rows,
         nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_gemm_dweight")
@@ -264,16 +271,16 @@ def logits_partials(logits: torch.Tensor, target: torch.Tensor | None, partials:
 
 
 def column_sums(x: torch.Tensor, out: torch.Tensor, *, rows: int, cols: int) -> None:
-    """out[c] <- sum_r x[r, c] for a bf16 [rows, >= cols] matrix, fp32 out (deterministic order)."""
+    """out[c] <- sum_r x[r, c] for a bf16 / fp16 [rows, >= cols] matrix, fp32 out (deterministic order)."""
     dev = _require_cuda(x, out)
     ld = _row_major(x, "x")
-    if x.dtype != torch.bfloat16:
-        raise TypeError("column_sums input must be bfloat16")
+    if x.dtype not in _GEMM_DTYPES:
+        raise TypeError("column_sums input must be bfloat16 or float16")
     if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < cols:
         raise ValueError("out must be contiguous float32 with >= cols elements")
     lib = nat.load()
-    rc = _launch("column_sums", dev, lambda: lib.frx_column_sums(x.data_ptr(), ld, rows, cols, out.data_ptr(),
-                                                                 nat.stream_of(dev)))
+    rc = _launch("column_sums", dev, lambda: lib.frx_column_sums(
+        x.data_ptr(), _GEMM_DTYPES[x.dtype], ld, rows, cols, out.data_ptr(), nat.stream_of(dev)))
     nat.check(rc, "frx_column_sums")
 
 
@@ -282,8 +289,7 @@ def gemm_dhidden_multicast(dz: torch.Tensor, weight: torch.Tensor, mc_ptr: int, 
     """Adds dz[rows, vocab_shard] @ weight[vocab_shard, H] into the fp32 matrix behind the NVLS
     multicast address `mc_ptr` (row stride ld_out): the cross-rank d_hidden sum inside the GEMM."""
     dev = _require_cuda(dz, weight)
-    if dz.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
-        raise TypeError("dz and weight must be bfloat16")
+    dt = _gemm_dtype(dz, weight)
     if not mc_ptr:
         raise ValueError("a multicast address is required")
     ldz = _row_major(dz, "dz")
@@ -291,7 +297,7 @@ def gemm_dhidden_multicast(dz: torch.Tensor, weight: torch.Tensor, mc_ptr: int, 
     hdim = weight.shape[1]
     lib = nat.load()
     rc = _launch("gemm_dhidden", dev, lambda: lib.frx_gemm_dhidden_multicast(
-        dz.data_ptr(), ldz, weight.data_ptr(), ldw, mc_ptr, ld_out, rows, hdim, vocab_shard,
+        dz.data_ptr(), ldz, weight.data_ptr(), ldw, dt, mc_ptr, ld_out, rows, hdim, vocab_shard,
         nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_gemm_dhidden_multicast")

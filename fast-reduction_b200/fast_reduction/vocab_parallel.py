@@ -101,18 +101,30 @@ def vocab_parallel_ce_entropy(
     (identical on every rank), shaped like hidden_states.shape[:-1]. ``bias_shard`` is the bias of
     this rank's vocabulary rows, if any."""
     batch_shape, hidden_2d, weight_shard, target_1d, bias_shard = gk._prepare(hidden_states, weight_shard, target,
-                                                                              bias_shard)
+                                                                              bias_shard, allow_host=True)
     B = hidden_2d.shape[0]
-    dev = hidden_2d.device
+    host_dev = gk._input_device(hidden_2d, weight_shard, target_1d, bias_shard)
+    dev = hidden_2d.device if host_dev is None else host_dev
     local = torch.empty(B, 4, device=dev, dtype=torch.float32)
-    gk.forward_stats(hidden_2d, weight_shard, target_1d, chunk_size, vocab_offset=vocab_start, merged=local,
-                     vocab_size=vocab_size, ignore_index=ignore_index, bias=bias_shard)
+    if host_dev is None:
+        gk.forward_stats(hidden_2d, weight_shard, target_1d, chunk_size, vocab_offset=vocab_start, merged=local,
+                         vocab_size=vocab_size, ignore_index=ignore_index, bias=bias_shard)
+        t_d = target_1d
+    else:
+        # Host inputs: each rank uploads 1/world of the hidden rows over its own PCIe link and the
+        # rows are all-gathered over NVLink, while the weight slice streams in under the GEMMs.
+        world = dist.get_world_size(group)
+        share = (dist.get_rank(group), world, lambda part: _gather_stats(part, group).view(-1, part.shape[1]))
+        t_d = target_1d.to(dev, non_blocking=True)
+        gk.forward_stats_from_host(hidden_2d, weight_shard, t_d, dev, bias=bias_shard, vocab_offset=vocab_start,
+                                   vocab_size=vocab_size, ignore_index=ignore_index, merged=local,
+                                   hidden_share=share if world > 1 else None)
     gathered = _gather_stats(local, group)
     ce = torch.empty(B, device=dev, dtype=torch.float32)
     ent = torch.empty(B, device=dev, dtype=torch.float32)
     logp = torch.empty(B, device=dev, dtype=torch.float32)
-    merge_rows(gathered, target_1d, vocab_size, ignore_index, ce=ce, entropy=ent, log_probs=logp)
-    return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
+    merge_rows(gathered, t_d, vocab_size, ignore_index, ce=ce, entropy=ent, log_probs=logp)
+    return gk._results_to(hidden_states.device, batch_shape, ce, ent, logp)
 
 
 def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, vocab_size, group, chunk_size,

@@ -13,7 +13,8 @@
  *     outside the vocabulary). The host reads it whenever it chooses to synchronise.
  *   - Vocabulary sharding: a call may cover only the slice [vocab_offset, vocab_offset +
  *     vocab_shard) of the vocabulary; `target` always holds global vocabulary ids.
- *   - bf16 operands need 16-byte aligned bases and leading dimensions that are multiples of 8.
+ *   - 16-bit operands (bf16, or fp16 where a `dtype` argument says so) need 16-byte aligned bases
+ *     and leading dimensions that are multiples of 8.
  *
  * The forward partials contract: for vocabulary tile t (columns [256 t, 256 t + 256) of the
  * shard) and row r, partials[t * tile_stride + r] holds four floats
@@ -37,7 +38,7 @@
 extern "C" {
 #endif
 
-#define FRX_ABI_VERSION 2
+#define FRX_ABI_VERSION 3
 
 #define FRX_OK 0
 #define FRX_ERR_INVALID_ARG 1
@@ -75,17 +76,18 @@ FRX_API const char* frx_last_error(void);
  * and, with `logits` non-NULL, the logits-writing variant `_gemm_ce_entropy_bwd_kernel`
  * (gemm_kernel.py:168-273, gemm_ce_entropy_bwd_epilogue.py:218).
  *
- *   z[r, j]  = sum_k hidden[r, k] * weight[j, k]        (bf16 x bf16 -> fp32, TMEM)
- *   hidden   [rows, hidden_dim] bf16, row stride ld_hidden
- *   weight   [vocab_shard, hidden_dim] bf16, row stride ld_weight (the shard's rows)
- *   bias     optional [vocab_shard] bf16 added to every logit of its column (z = x W^T + b, as the
+ *   z[r, j]  = sum_k hidden[r, k] * weight[j, k]        (16-bit x 16-bit -> fp32, TMEM)
+ *   dtype    FRX_DTYPE_BF16 or FRX_DTYPE_F16: the type of hidden, weight and bias
+ *   hidden   [rows, hidden_dim], row stride ld_hidden
+ *   weight   [vocab_shard, hidden_dim], row stride ld_weight (the shard's rows)
+ *   bias     optional [vocab_shard] added to every logit of its column (z = x W^T + b, as the
  *            reference's fp32 baseline computes; the reference's own GEMM path ignores bias)
  *   target   [rows] int64 global ids, or NULL (then zt = 0)
  *   partials [ceil(vocab_shard / 256) * tile_stride] x float4, tile_stride >= rows
  *   logits   optional fp32 [rows, ld_logits] output of every z (NULL: logits never leave the chip)
  */
 FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
-                     const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
+                     int dtype, const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
                      int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
                      int64_t ld_logits, int* status, void* stream);
 
@@ -112,7 +114,7 @@ FRX_API int frx_finalize(const float* partials, int64_t n_tiles, int64_t rows, i
  *   p = exp(z - lse);  dz = p * (g_ce - g_ent * (log p + H)) - g_ce * [j == target]
  * Replaces `ComputeDlogits` / `compute_dlogits` (fast_reduction/cute_dlogits.py:32-100, 162-183).
  * g_ce / g_ent: per-row fp32 vectors, or NULL to use the scalars ce_weight / ent_weight.
- * Rows with target == ignore_index drop the CE term. out_dtype: FRX_DTYPE_BF16 or _F32.
+ * Rows with target == ignore_index drop the CE term. out_dtype: FRX_DTYPE_BF16, _F16 or _F32.
  */
 FRX_API int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t* target, const float* lse,
                 const float* entropy, const float* g_ce, const float* g_ent, float ce_weight,
@@ -121,11 +123,12 @@ FRX_API int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t* t
 
 /*
  * d_hidden[rows, hidden_dim] = dlogits[rows, vocab_shard] @ weight[vocab_shard, hidden_dim]
- * (bf16 in, fp32 accumulation, out_dtype out). Replaces the cuBLAS `torch.mm(dlogits, weight)`
- * of the reference's megakernel (fast_reduction/gemm_kernel.py:859-862).
+ * (in_dtype = FRX_DTYPE_BF16 or _F16 for both inputs, fp32 accumulation, out_dtype out: BF16, F16
+ * or F32). Replaces the cuBLAS `torch.mm(dlogits, weight)` of the reference's megakernel
+ * (fast_reduction/gemm_kernel.py:859-862).
  */
 FRX_API int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void* weight, int64_t ld_weight,
-                     void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows, int64_t hidden_dim,
+                     int in_dtype, void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows, int64_t hidden_dim,
                      int64_t vocab_shard, int* status, void* stream);
 
 /*
@@ -139,25 +142,28 @@ FRX_API int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void
  * fast_reduction/gemm_kernel.py:859-862).
  */
 FRX_API int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogits, const void* weight,
-                                       int64_t ld_weight, void* d_hidden_mc, int64_t ld_d_hidden, int64_t rows,
-                                       int64_t hidden_dim, int64_t vocab_shard, int* status, void* stream);
+                                       int64_t ld_weight, int in_dtype, void* d_hidden_mc, int64_t ld_d_hidden,
+                                       int64_t rows, int64_t hidden_dim, int64_t vocab_shard, int* status,
+                                       void* stream);
 
 /*
  * d_weight[vocab_shard, hidden_dim] = dlogits[rows, vocab_shard]^T @ hidden[rows, hidden_dim]
- * accumulated over all `rows` in fp32 tensor memory and written once in out_dtype. Replaces
+ * (in_dtype = FRX_DTYPE_BF16 or _F16 for both inputs) accumulated over all `rows` in fp32 tensor
+ * memory and written once in out_dtype (BF16, F16 or F32). Replaces
  * the per-chunk `d_weight.add_(torch.mm(dlogits.t(), h_chunk).float())` and the final cast
  * of the reference (fast_reduction/gemm_kernel.py:864-871).
  */
 FRX_API int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
-                     void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
+                     int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
                      int64_t hidden_dim, int64_t rows, int* status, void* stream);
 
 /*
- * Column sums out[c] = sum_r x[r, c] (fp32 accumulation, fixed order, so deterministic) of a bf16
- * matrix [rows, cols] with row stride ld: the bias gradient from the dlogits of one shard.
+ * Column sums out[c] = sum_r x[r, c] (fp32 accumulation, fixed order, so deterministic) of a bf16 or
+ * fp16 (dtype) matrix [rows, cols] with row stride ld: the bias gradient from the dlogits of one shard.
  * Replaces the reference's `d_bias.add_(dlogits.sum(dim=0))` (fast_reduction/gemm_kernel.py:867-869).
  */
-FRX_API int frx_column_sums(const void* x, int64_t ld, int64_t rows, int64_t cols, float* out, void* stream);
+FRX_API int frx_column_sums(const void* x, int dtype, int64_t ld, int64_t rows, int64_t cols, float* out,
+                            void* stream);
 
 /*
  * Softmax partials of a materialised logits matrix [rows, cols] (dtype FRX_DTYPE_BF16, _F16 or

@@ -67,6 +67,18 @@ def main() -> None:
                chunked_target=t.numpy(), chunked_chunk=np.int64(chunk),
                chunked_ce=ce.numpy(), chunked_ent=ent.numpy(), chunked_lp=lp.numpy())
 
+    # 2b. The same chunked path on fp16 inputs (the reference's matmul runs in the input dtype, so its
+    #     logits are rounded to fp16 before the fp32 reduction).
+    torch.manual_seed(8)
+    B, H, V, chunk = 72, 64, 1000, 32
+    h = torch.randn(B, H).to(torch.float16)
+    w = (torch.randn(V, H) / math.sqrt(H)).to(torch.float16)
+    t = torch.randint(0, V, (B,))
+    ce, ent, lp = ref.chunked_linear_xent_entropy(h, w, t, chunk_size=chunk)
+    out.update(chunked16_hidden=h.view(torch.int16).numpy(), chunked16_weight=w.view(torch.int16).numpy(),
+               chunked16_target=t.numpy(), chunked16_chunk=np.int64(chunk),
+               chunked16_ce=ce.numpy(), chunked16_ent=ent.numpy(), chunked16_lp=lp.numpy())
+
     # 3. fp32 autograd ground truth for gradients (baseline.py:91-150), default g_ce=1, g_ent=-1,
     #    and with per-row upstream gradients.
     torch.manual_seed(123)
@@ -92,6 +104,18 @@ def main() -> None:
     ce, ent, dh, dw, db = ref.baseline_linear_xent_entropy_backward(h, w, t, bias=b)
     out.update(bias_hidden=h.numpy(), bias_weight=w.numpy(), bias_bias=b.numpy(), bias_target=t.numpy(),
                bias_ce=ce.numpy(), bias_ent=ent.numpy(), bias_dh=dh.numpy(), bias_dw=dw.numpy(), bias_db=db.numpy())
+
+    # 3c. fp16 inputs through the reference's backward: it differentiates in fp32 and casts the
+    #     gradients back to fp16 (baseline.py:140-141).
+    torch.manual_seed(654)
+    B, H, V = 40, 64, 500
+    h = torch.randn(B, H).to(torch.float16)
+    w = (torch.randn(V, H) * 0.2).to(torch.float16)
+    t = torch.randint(0, V, (B,))
+    ce, ent, dh, dw, _ = ref.baseline_linear_xent_entropy_backward(h, w, t)
+    out.update(bwd16_hidden=h.view(torch.int16).numpy(), bwd16_weight=w.view(torch.int16).numpy(),
+               bwd16_target=t.numpy(), bwd16_ce=ce.numpy(), bwd16_ent=ent.numpy(),
+               bwd16_dh=dh.view(torch.int16).numpy(), bwd16_dw=dw.view(torch.int16).numpy())
 
     # 4. BASELINE configs[0] (B=1024, H=1024, V=32000, chunk 512, seed 0): inputs are regenerated
     #    from the seed at test time (checked by digest); only the reference's outputs are stored.

@@ -61,26 +61,35 @@ def test_invalid_arguments_return_codes_without_gpu():
 
     lib = nat.load()
     # negative sizes are rejected before any CUDA call
-    rc = lib.frx_fwd_partials(None, 0, None, 0, None, None, -1, 10, 64, 0, None, 0, None, 0, None, None)
+    rc = lib.frx_fwd_partials(None, 0, None, 0, 0, None, None, -1, 10, 64, 0, None, 0, None, 0, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG
     assert b"bad sizes" in lib.frx_last_error()
-    rc = lib.frx_fwd_partials(1 << 20, 64, 1 << 21, 64, None, None, 8, 10, 60, 0, 1 << 22, 8, None, 0, None, None)
+    rc = lib.frx_fwd_partials(1 << 20, 64, 1 << 21, 64, 0, None, None, 8, 10, 60, 0, 1 << 22, 8, None, 0, None, None)
     assert rc == nat.FRX_ERR_UNSUPPORTED  # hidden_dim not a multiple of 8
+    rc = lib.frx_fwd_partials(1 << 20, 64, 1 << 21, 64, nat.FRX_DTYPE_F32, None, None, 8, 10, 64, 0, 1 << 22, 8,
+                              None, 0, None, None)
+    assert rc == nat.FRX_ERR_UNSUPPORTED  # fp32 operands: the GEMM core takes bf16 or fp16
+    assert b"dtype" in lib.frx_last_error()
     rc = lib.frx_finalize(None, 3, 10, 5, 0, None, 0, 0, None, None, None, None, None, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG  # tile_stride < rows
     rc = lib.frx_finalize(None, 1, 10, 10, 0x40, None, 0, 0, None, None, None, None, None, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG  # unknown flag
     rc = lib.frx_dlogits(None, 0, None, None, None, None, None, 1.0, -1.0, None, 0, 7, 4, 4, 0, 0, None)
     assert rc == nat.FRX_ERR_INVALID_ARG
-    rc = lib.frx_gemm_dhidden(None, 0, None, 0, None, 0, 0, -5, 64, 64, None, None)
+    rc = lib.frx_gemm_dhidden(None, 0, None, 0, 0, None, 0, 0, -5, 64, 64, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG
-    rc = lib.frx_gemm_dweight(None, 0, None, 0, None, 0, 0, 64, 64, 0, None, None)
+    rc = lib.frx_gemm_dweight(None, 0, None, 0, 0, None, 0, 0, 64, 64, 0, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG
+    rc = lib.frx_column_sums(1 << 20, nat.FRX_DTYPE_F32, 8, 4, 8, 1 << 21, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # column sums read 16-bit matrices only
+    rc = lib.frx_dlogits(1 << 20, 8, None, 1 << 21, 1 << 21, None, None, 1.0, -1.0, 1 << 22, 8, 9, 4, 4, 0, 0, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # unknown out_dtype
 
 
 def test_empty_problems_are_noops():
     from fast_reduction import _native as nat
 
     lib = nat.load()
-    assert lib.frx_fwd_partials(None, 0, None, 0, None, None, 0, 10, 64, 0, None, 0, None, 0, None, None) == nat.FRX_OK
+    assert lib.frx_fwd_partials(None, 0, None, 0, 0, None, None, 0, 10, 64, 0, None, 0, None, 0, None,
+                                None) == nat.FRX_OK
     assert lib.frx_finalize(None, 0, 0, 0, 0, None, 0, 0, None, None, None, None, None, None, None) == nat.FRX_OK

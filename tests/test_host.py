@@ -17,23 +17,42 @@ def _inputs(dtype=torch.bfloat16, B=8, H=16, V=40):
 def test_cpu_tensors_rejected_no_fallback():
     h, w, t = _inputs()
     with pytest.raises(ValueError, match="CUDA"):
-        gk.gemm_fused_ce_entropy(h, w, t)
-    with pytest.raises(ValueError, match="CUDA"):
         gk.gemm_megakernel_fast(h, w, t)
+    if not torch.cuda.is_available():
+        # host inputs are streamed to a GPU, never computed on the CPU
+        with pytest.raises(RuntimeError, match="CUDA device"):
+            gk.gemm_fused_ce_entropy(h, w, t)
+
+
+def test_host_input_device_rules():
+    h, w, t = _inputs()
+    assert gk._input_device(None, None) is None
+    meta = torch.empty(4, device="meta")
+    with pytest.raises(ValueError, match="CUDA or CPU"):
+        gk._input_device(h, meta)
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="CUDA device"):
+            gk._input_device(h, w, t)
 
 
 def test_bias_checks():
     h, w, t = _inputs()
     with pytest.raises(ValueError, match="bias must be"):
         gk.gemm_fused_ce_entropy(h, w, t, bias=torch.zeros(39, dtype=torch.bfloat16))
-    with pytest.raises(NotImplementedError, match="bf16"):
+    with pytest.raises(NotImplementedError, match="weight's dtype"):
         gk.gemm_fused_ce_entropy(h, w, t, bias=torch.zeros(40))
 
 
-def test_non_bf16_rejected():
+def test_unsupported_dtypes_rejected():
     h, w, t = _inputs(dtype=torch.float32)
-    with pytest.raises(NotImplementedError, match="bf16"):
+    with pytest.raises(NotImplementedError, match="bf16 or fp16"):
         gk.gemm_fused_ce_entropy(h, w, t)
+    h, w, t = _inputs()
+    with pytest.raises(NotImplementedError, match="same type"):
+        gk.gemm_fused_ce_entropy(h, w.to(torch.float16), t)
+    with pytest.raises(TypeError, match="all be bfloat16 or all float16"):
+        ops._gemm_dtype(h, w.to(torch.float16))
+    assert ops._gemm_dtype(h.half(), w.half()) == ops.nat.FRX_DTYPE_F16
 
 
 def test_shape_checks():

@@ -36,6 +36,33 @@ def test_chunked_restatement_matches_reference_bitwise():
     assert torch.equal(lp, torch.from_numpy(g["chunked_lp"]))
 
 
+def test_chunked_restatement_matches_reference_bitwise_fp16():
+    g = GOLDEN
+    h = torch.from_numpy(g["chunked16_hidden"]).view(torch.float16)
+    w = torch.from_numpy(g["chunked16_weight"]).view(torch.float16)
+    t = torch.from_numpy(g["chunked16_target"])
+    ce, ent, lp = rm.chunked_linear_xent_entropy(h, w, t, chunk_size=int(g["chunked16_chunk"]))
+    assert torch.equal(ce, torch.from_numpy(g["chunked16_ce"]))
+    assert torch.equal(ent, torch.from_numpy(g["chunked16_ent"]))
+    assert torch.equal(lp, torch.from_numpy(g["chunked16_lp"]))
+
+
+def test_grads_restatement_matches_reference_autograd_fp16_inputs():
+    """fp16 inputs: the reference differentiates in fp32 and casts the gradients to fp16."""
+    g = GOLDEN
+    h = torch.from_numpy(g["bwd16_hidden"]).view(torch.float16)
+    w = torch.from_numpy(g["bwd16_weight"]).view(torch.float16)
+    t = torch.from_numpy(g["bwd16_target"])
+    ce, ent, dh, dw = rm.fp32_reference_grads(h, w, t)
+    np.testing.assert_allclose(ce.numpy(), g["bwd16_ce"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(ent.numpy(), g["bwd16_ent"], rtol=1e-5, atol=1e-6)
+    ref_dh = torch.from_numpy(g["bwd16_dh"]).view(torch.float16)
+    ref_dw = torch.from_numpy(g["bwd16_dw"]).view(torch.float16)
+    # one fp16 rounding apart at most
+    assert (dh.half().float() - ref_dh.float()).abs().max() <= 1e-3 * ref_dh.float().abs().max()
+    assert (dw.half().float() - ref_dw.float()).abs().max() <= 1e-3 * ref_dw.float().abs().max()
+
+
 def test_grads_restatement_matches_reference_autograd():
     g = GOLDEN
     h, w, t = (torch.from_numpy(g[k]) for k in ("bwd_hidden", "bwd_weight", "bwd_target"))

@@ -49,6 +49,11 @@ def _worker(rank, world, port, q, nvls):
                                                 bias_shard=bias[a:b].to(dev))
         ce1, ent1, lp1 = gemm_fused_ce_entropy(hd, w.to(dev), td, bias=bias.to(dev), chunk_size=chunk)
         err_fwd = max(float((ce - ce1).abs().max()), float((ent - ent1).abs().max()), float((lp - lp1).abs().max()))
+        # host inputs: each rank uploads a share of the hidden rows, all-gathers them, streams its weight slice
+        host = vocab_parallel_ce_entropy(h.pin_memory(), w[a:b].pin_memory(), t.pin_memory(), a, V,
+                                         chunk_size=chunk, bias_shard=bias[a:b].pin_memory())
+        if not all(x.device.type == "cpu" and torch.equal(x, y.cpu()) for x, y in zip(host, (ce, ent, lp))):
+            err_fwd = float("inf")
 
         h_leaf = h.to(dev).requires_grad_(True)
         w_leaf = w[a:b].to(dev).requires_grad_(True)
