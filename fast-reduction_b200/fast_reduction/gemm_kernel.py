@@ -435,7 +435,8 @@ def fwd_bwd_shard(
 
     For each row chunk: GEMM epilogue writes the chunk's fp32 logits (and partials); the
     per-row lse / entropy of the chunk are produced by ``stats_fn(start, end, partials, T, chunk)``
-    (single GPU: a local finalize; vocabulary-parallel: local merge + cross-rank exchange);
+    (single GPU: a local finalize; vocabulary-parallel: local merge + cross-rank exchange), which
+    runs on the side stream with the chunk's dlogits when there are several chunks;
     frx_dlogits writes the chunk's dlogits (in the operands' 16-bit type) into a [B, V_shard] buffer. Then one
     d_hidden GEMM and one d_weight GEMM over all rows.
     """
@@ -444,13 +445,14 @@ def fwd_bwd_shard(
     dev = hidden_2d.device
     chunk = _chunk_rows(chunk_size, B)
     T = ops.n_vocab_tiles(V)
-    partials = torch.empty(T, chunk, 4, device=dev, dtype=torch.float32)
     n_chunks = (B + chunk - 1) // chunk
     overlap = _OVERLAP_DLOGITS and n_chunks > 1
-    # Two logits buffers when the dlogits of chunk c (HBM-bound) runs on a side stream under the
-    # forward GEMM of chunk c+1 (tensor-bound); the GEMM of chunk c+2 waits for it.
-    logits_bufs = [torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32)
-                   for _ in range(2 if overlap else 1)]
+    # Two logits (and partials) buffers when the statistics and dlogits of chunk c run on a side
+    # stream under the forward GEMM of chunk c+1 (tensor-bound); the GEMM of chunk c+2 waits for
+    # them. The main stream then never waits on a cross-rank statistics exchange.
+    n_buf = 2 if overlap else 1
+    logits_bufs = [torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32) for _ in range(n_buf)]
+    partials_bufs = [torch.empty(T, chunk, 4, device=dev, dtype=torch.float32) for _ in range(n_buf)]
     dz = torch.empty(B, ops.round_up(V, 8), device=dev, dtype=hidden_2d.dtype)
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev) if overlap else None
@@ -460,15 +462,15 @@ def fwd_bwd_shard(
     for c, start in enumerate(range(0, B, chunk)):
         end = min(start + chunk, B)
         rows = end - start
-        buf = c % len(logits_bufs)
-        logits = logits_bufs[buf]
+        buf = c % n_buf
+        logits, partials = logits_bufs[buf], partials_bufs[buf]
         if done[buf] is not None:
             main.wait_event(done[buf])
         ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
                          logits=logits, bias=bias)
-        stats_fn(start, end, partials, T, chunk)
 
-        def run_dlogits(logits=logits, start=start, end=end, rows=rows):
+        def run_dlogits(logits=logits, partials=partials, start=start, end=end, rows=rows):
+            stats_fn(start, end, partials, T, chunk)
             ops.dlogits(
                 logits, target_1d[start:end], lse[start:end], entropy[start:end], dz[start:end],
                 rows=rows, vocab_shard=V, ce_weight=ce_weight, ent_weight=ent_weight,
@@ -490,10 +492,10 @@ def fwd_bwd_shard(
             done[buf] = ev
     if side is not None:
         main.wait_stream(side)
-        for t_ in logits_bufs + [dz, lse, entropy, target_1d, g_ce, g_ent]:
+        for t_ in logits_bufs + partials_bufs + [dz, lse, entropy, target_1d, g_ce, g_ent]:
             if t_ is not None:
                 t_.record_stream(side)
-    del logits_bufs, partials
+    del logits_bufs, partials_bufs, partials
     if dhidden_fn is not None:
         d_hidden, pending = dhidden_fn(dz)
     else:
