@@ -8,6 +8,7 @@ The same line also reports the training step (`gemm_megakernel_fast` + loss.back
 under "fwd_bwd".
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --micro        (HBM-bound kernels alone: finalize, dlogits, column sums, CE over logits)
     torchrun --nproc-per-node N bench.py --gpus N ...      (vocabulary sharded over N GPUs)
 
 Timing: CUDA events on the launching stream, barrier + synchronize on both sides, max over ranks.
@@ -307,7 +308,11 @@ def run_ours(args, world, rank, local):
     # ---- forward (headline value) with per-kernel event timing and clock sampling
     timer = KernelTimer()
     sampler = ClockSampler(local)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.cuda.reset_peak_memory_stats(dev)
+    mem_base = torch.cuda.memory_allocated(dev)
     fwd_ms, clocks = time_steps(fwd, args.steps, args.warmup, world, timer, sampler)
+    peak_extra_fwd = (torch.cuda.max_memory_allocated(dev) - mem_base) / 1e9
     ksum = timer.summary()
     launches_fwd = timer.count
     flops_fwd = 2.0 * B * H * V
@@ -355,7 +360,10 @@ def run_ours(args, world, rank, local):
 
         timer_fb = KernelTimer()
         fb_steps = max(1, min(args.steps, 10))
+        torch.cuda.reset_peak_memory_stats(dev)
+        mem_base_fb = torch.cuda.memory_allocated(dev)
         fb_ms, fb_clocks = time_steps(train_step, fb_steps, max(args.warmup, 1), world, timer_fb, ClockSampler(local))
+        peak_extra_fb = (torch.cuda.max_memory_allocated(dev) - mem_base_fb) / 1e9
         kfb = timer_fb.summary()
         flops_fb = 6.0 * B * H * V
         fb = {"ms": round(fb_ms, 3), "tflops": round(flops_fb / (fb_ms / 1000.0) / 1e12, 1),
@@ -363,6 +371,7 @@ def run_ours(args, world, rank, local):
               "frac_of_sustained_peak": round(flops_fb / (fb_ms / 1000.0) / 1e12 / (peak_sus * world), 4),
               "steps": fb_steps,
               "workload": "configs[2] gemm_megakernel_fast + loss.backward(), ce_weight 1, ent_weight -1",
+              "peak_extra_mem_gb": round(peak_extra_fb, 3),
               "kernels_ms_per_step": {k: round(v["total_ms"] / fb_steps, 3) for k, v in kfb.items()},
               "gpu_launches_per_step": timer_fb.count // fb_steps, "clocks": fb_clocks}
         if world == 1:
@@ -454,6 +463,7 @@ def run_ours(args, world, rank, local):
                      "launches_timed": gemm["launches"]},
         "kernels_ms_per_step": {k: round(v["total_ms"] / args.steps, 4) for k, v in ksum.items()},
         "gpu_launches": launches_fwd,
+        "peak_extra_mem_gb": round(peak_extra_fwd, 3),
         "clocks": clocks,
         "accuracy": acc,
         "fwd_bwd": fb,
@@ -461,6 +471,76 @@ def run_ours(args, world, rank, local):
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
+
+
+def run_micro(args):
+    """--micro: each HBM-bound libfrx kernel alone on inputs larger than L2, timed with CUDA events on
+    the launching stream; one JSON line per kernel with its algorithmic bytes and achieved GB/s."""
+    from fast_reduction import ops
+
+    peaks = load_peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1)
+
+    def timeit(fn, iters=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / iters
+
+    def report(kernel, shape, ms, nbytes, note):
+        gbs = nbytes / (ms / 1000.0) / 1e9
+        print(json.dumps({"micro": kernel, "shape": shape, "ms": round(ms, 4), "algorithmic_bytes": int(nbytes),
+                          "achieved_gbs": round(gbs, 1), "peak_gbs": hbm, "frac_of_hbm_peak": round(gbs / hbm, 4),
+                          "peak_source": peaks.get("source"), "bytes": note}), flush=True)
+
+    # finalize: partials of all 32768 rows over the 501 vocabulary tiles of V=128256 (the host-streamed
+    # forward's single finalize), 16 B per (tile, row) in, 12 B per row out (ce, entropy, log_probs).
+    sc = max(1, args.micro_scale)
+    T, R = ops.n_vocab_tiles(128256), 32768
+    part = torch.randn(T, R, 4, device=dev, generator=g).abs_() + 1.0
+    tgt = torch.randint(0, 128256, (R,), device=dev, generator=g)
+    outs = [torch.empty(R, device=dev) for _ in range(3)]
+    ms = timeit(lambda: ops.finalize(part, T, R, R, target=tgt, vocab_size=128256, ce=outs[0], entropy=outs[1],
+                                     log_probs=outs[2]))
+    report("finalize", [T, R], ms, T * R * 16 + R * (8 + 12), "16 B per (tile, row) + 8 B target + 12 B out per row")
+    del part, outs
+
+    # dlogits: one 4096-row chunk of the headline training step (fp32 logits in, bf16 dlogits out).
+    M, V = 4096 // sc, 128256
+    ld = ops.round_up(V, 4)
+    z = torch.randn(M, ld, device=dev, generator=g)
+    lse = torch.full((M,), 12.0, device=dev)
+    ent = torch.full((M,), 10.0, device=dev)
+    tg = torch.randint(0, V, (M,), device=dev, generator=g)
+    dz = torch.empty(M, ops.round_up(V, 8), device=dev, dtype=torch.bfloat16)
+    ms = timeit(lambda: ops.dlogits(z, tg, lse, ent, dz, rows=M, vocab_shard=V))
+    report("dlogits", [M, V], ms, M * V * 6 + M * 16, "4 B logit read + 2 B dlogit write per element + row stats")
+    del z
+
+    # column sums: d_bias of the headline training step (bf16 dlogits [32768, 128256] -> fp32 [V]).
+    R2 = 32768 // sc
+    big = torch.empty(R2, ops.round_up(V, 8), device=dev, dtype=torch.bfloat16).normal_(generator=g)
+    db = torch.empty(V, device=dev)
+    ms = timeit(lambda: ops.column_sums(big, db, rows=R2, cols=V), iters=5)
+    report("column_sums", [R2, V], ms, R2 * V * 2 + V * 4, "2 B per element read + 4 B per column written")
+    del big, dz
+
+    # standalone CE / entropy over materialised bf16 logits [32768, 32000] (configs[0]'s vocabulary).
+    M3, N3 = 32768 // sc, 32000
+    logits = torch.empty(M3, N3, device=dev, dtype=torch.bfloat16).normal_(generator=g)
+    tg3 = torch.randint(0, N3, (M3,), device=dev, generator=g)
+    from fast_reduction.cute_cross_entropy import ce_entropy_fwd
+    ms = timeit(lambda: ce_entropy_fwd(logits, tg3))
+    report("logits_partials+finalize (ce_entropy_fwd)", [M3, N3], ms, M3 * N3 * 2 + M3 * 16,
+           "2 B per logit read + 8 B target + 8 B out per row")
 
 
 def main():
@@ -476,7 +556,12 @@ def main():
     ap.add_argument("--no-fwd-bwd", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--micro", action="store_true", help="time the HBM-bound kernels alone (one line each)")
+    ap.add_argument("--micro-scale", type=int, default=1, help="divide the --micro row counts (small ncu cases)")
     args = ap.parse_args()
+    if args.micro:
+        run_micro(args)
+        return
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

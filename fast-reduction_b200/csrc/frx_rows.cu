@@ -34,24 +34,35 @@ __device__ __forceinline__ void online_merge(OnlineStat& a, const OnlineStat& b)
   a.m = M;
 }
 
+// Adds n_valid values to the running stats. The reference point m only moves up when a vector
+// holds a larger value (rare after the first few vectors of a row), so the steady state costs one
+// ex2 per element; a raise rescales s and u to the new m first:
+//   s' = s e^(m - M),  u' = (u + (m - M) s) e^(m - M).
 template <int N>
 __device__ __forceinline__ void online_add(OnlineStat& st, const float (&v)[N], int n_valid) {
   float vm = -INFINITY;
 #pragma unroll
   for (int i = 0; i < N; ++i)
     if (i < n_valid) vm = fmaxf(vm, v[i]);
+  if (vm > st.m) {
+    if (st.m != -INFINITY) {
+      const float d = st.m - vm;
+      const float e = ex2_approx(d * kLog2e);
+      st.u = fmaf(d, st.s, st.u) * e;
+      st.s *= e;
+    }
+    st.m = vm;
+  }
   if (vm == -INFINITY) return;
-  OnlineStat b{vm, 0.f, 0.f};
-  const float ml = vm * kLog2e;
+  const float ml = st.m * kLog2e;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     if (i < n_valid) {
       const float e = ex2_approx(fmaf(v[i], kLog2e, -ml));
-      b.s += e;
-      b.u = fmaf(v[i] - vm, e, b.u);
+      st.s += e;
+      st.u = fmaf(v[i] - st.m, e, st.u);
     }
   }
-  online_merge(st, b);
 }
 
 template <typename T>
@@ -110,8 +121,17 @@ __global__ void __launch_bounds__(kRowThreads)
     const T* xr = x + row * ld;
     OnlineStat st{-INFINITY, 0.f, 0.f};
     if (vec_ok) {
-      for (int64_t c = c_begin + static_cast<int64_t>(threadIdx.x) * N; c < c_end;
-           c += static_cast<int64_t>(kRowThreads) * N) {
+      constexpr int64_t kStride = static_cast<int64_t>(kRowThreads) * N;
+      int64_t c = c_begin + static_cast<int64_t>(threadIdx.x) * N;
+      // two full vectors per step, both loads issued before the math (same element order as below)
+      for (; c + kStride + N <= c_end; c += 2 * kStride) {
+        float a[N], b[N];
+        V::load(xr + c, a);
+        V::load(xr + c + kStride, b);
+        online_add<N>(st, a, N);
+        online_add<N>(st, b, N);
+      }
+      for (; c < c_end; c += kStride) {
         float v[N];
         if (c + N <= c_end) {
           V::load(xr + c, v);
@@ -192,6 +212,23 @@ extern "C" int frx_logits_partials(const void* logits, int dtype, int64_t ld, in
 
 namespace frx {
 
+// acc[i] += the 8 16-bit values of q (bf16, or fp16 when kF16).
+template <bool kF16>
+__device__ __forceinline__ void add8(float (&acc)[8], const uint4& q) {
+  const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (kF16) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      acc[2 * i] += f.x;
+      acc[2 * i + 1] += f.y;
+    } else {
+      acc[2 * i] += __uint_as_float(w[i] << 16);
+      acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+}
+
 // out[c] = sum over rows of x[r, c] (x bf16, or fp16 when kF16): a CTA owns 256 columns (8 per
 // lane, 16-byte loads); its 8 warps take every 8th row, four rows in flight each, and the per-warp
 // sums are added in a fixed order through shared memory.
@@ -206,22 +243,22 @@ __global__ void __launch_bounds__(256)
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   if (c0 < cols) {
     const bool full = vec_ok && c0 + 8 <= cols;
-    for (int64_t r = warp; r < rows; r += 8) {
+    int64_t r = warp;
+    if (full) {
+      // four rows per step with all four loads issued first; rows are added in increasing order,
+      // exactly as the one-row loop below would add them
+      for (; r + 24 < rows; r += 32) {
+        uint4 q[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) q[k] = __ldcs(reinterpret_cast<const uint4*>(x + (r + 8 * k) * ld + c0));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) add8<kF16>(acc, q[k]);
+      }
+    }
+    for (; r < rows; r += 8) {
       const uint16_t* xr = x + r * ld + c0;
       if (full) {
-        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(xr));
-        const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          if (kF16) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-            acc[2 * i] += f.x;
-            acc[2 * i + 1] += f.y;
-          } else {
-            acc[2 * i] += __uint_as_float(w[i] << 16);
-            acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
-          }
-        }
+        add8<kF16>(acc, __ldcs(reinterpret_cast<const uint4*>(xr)));
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
