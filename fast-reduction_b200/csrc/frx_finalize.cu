@@ -8,7 +8,7 @@
 //
 // Merge rule (associative; identical to the reference's online-softmax merge in
 // fast_reduction/gemm_ce_entropy_finalize.py:78-92, restated for the centred third slot):
-//   M = max(m_a, m_b), a = exp(m_a - M), b = exp(m_b - M)
+//   M = max(m_a, m_b), a = exp(m_a - M), b = exp(m_b - M)   (one of the two is exactly 1)
 //   S = s_a a + s_b b,  U = (u_a + (m_a - M) s_a) a + (u_b + (m_b - M) s_b) b,  ZT = zt_a + zt_b
 // Final: lse = M + log S, H = log S - U / S, ce = lse - ZT (reference: :94-97).
 #include <cmath>
@@ -31,13 +31,17 @@ __device__ __forceinline__ RowStat merge_stats(RowStat a, const RowStat& b) {
     r.zt += a.zt;
     return r;
   }
-  const float M = fmaxf(a.m, b.m);
-  const float da = a.m - M, db = b.m - M;
-  const float ea = expf(da), eb = expf(db);
+  // Only the smaller of the two maxima needs rescaling: one exp per merge, no branch.
+  const bool a_hi = a.m >= b.m;
+  const float m_hi = a_hi ? a.m : b.m, m_lo = a_hi ? b.m : a.m;
+  const float s_hi = a_hi ? a.s : b.s, s_lo = a_hi ? b.s : a.s;
+  const float u_hi = a_hi ? a.u : b.u, u_lo = a_hi ? b.u : a.u;
+  const float d = m_lo - m_hi;  // <= 0
+  const float e = ex2_approx(d * kLog2e);
   RowStat r;
-  r.m = M;
-  r.s = a.s * ea + b.s * eb;
-  r.u = fmaf(da, a.s, a.u) * ea + fmaf(db, b.s, b.u) * eb;
+  r.m = m_hi;
+  r.s = fmaf(s_lo, e, s_hi);
+  r.u = fmaf(fmaf(d, s_lo, u_lo), e, u_hi);
   r.zt = a.zt + b.zt;
   return r;
 }
@@ -123,7 +127,8 @@ extern "C" int frx_finalize(const float* partials, int64_t n_tiles, int64_t rows
   FRX_REQUIRE(blocks < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_finalize: too many rows");
   finalize_kernel<<<static_cast<unsigned>(blocks), kFinRows * kFinSplits, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const float4*>(partials), n_tiles, rows, tile_stride, (flags & FRX_PARTIALS_REF_LAYOUT) ? 1 : 0,
-      (flags & FRX_IGNORE_NEGATIVE_TARGETS) ? 1 : 0, target, vocab_size, ignore_index, ce, entropy, lse, log_probs, reinterpret_cast<float4*>(merged), status);
+      (flags & FRX_IGNORE_NEGATIVE_TARGETS) ? 1 : 0, target, vocab_size, ignore_index, ce, entropy, lse, log_probs,
+      reinterpret_cast<float4*>(merged), status);
   FRX_CUDA_CHECK(cudaGetLastError());
   return FRX_OK;
 }

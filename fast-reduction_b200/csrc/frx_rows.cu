@@ -1,10 +1,10 @@
 // Softmax partials of given logits (no GEMM): the standalone cross-entropy / entropy /
 // logsumexp reductions over a materialised [rows, cols] logits matrix.
 //
-// One CTA reduces one (row, column tile) to the same (m, s, u, zt) partial the fused GEMM
+// One warp reduces one (row, column tile) to the same (m, s, u, zt) partial the fused GEMM
 // epilogue writes, so frx_finalize produces ce / entropy / lse from it, and a long row is
-// spread over several CTAs when there are few rows. Each thread streams 16-byte vectors and
-// keeps an online (max, sum exp, sum (x - max) exp) over them; the CTA merges its 8 warps.
+// spread over several warps when there are few rows. Each lane streams 16-byte vectors and
+// keeps an online (max, sum exp, sum (x - max) exp) over them; shuffles merge the lanes.
 // HBM-bound: cols * sizeof(T) bytes read per row.
 // Reference: fast_reduction/cute_cross_entropy.py:171-578 (CrossEntropyOnly, EntropyOnly,
 // CrossEntropyEntropy), wrappers :583-735.
@@ -106,6 +106,9 @@ struct Vec16<__half> {
   __device__ static float scalar(const __half* p) { return __half2float(*p); }
 };
 
+// One warp reduces one (row, column tile): each lane streams 16-byte vectors (two loads in flight)
+// into its own online stats, then five shuffle merges combine the lanes. No shared memory and no
+// block barrier, so short tiles (a few thousand columns) cost no more per byte than long ones.
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads)
     logits_partials_kernel(const T* __restrict__ x, int64_t ld, int64_t rows, int64_t cols,
@@ -113,16 +116,18 @@ __global__ void __launch_bounds__(kRowThreads)
                            int64_t tile_stride, int vec_ok) {
   using V = Vec16<T>;
   constexpr int N = V::N;
-  __shared__ OnlineStat red[kRowThreads / 32];
+  constexpr int kWarps = kRowThreads / 32;
+  const int lane = threadIdx.x & 31;
   const int64_t tile = blockIdx.x;
   const int64_t c_begin = tile * tile_cols;
   const int64_t c_end = min(cols, c_begin + tile_cols);
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
+  for (int64_t row = static_cast<int64_t>(blockIdx.y) * kWarps + (threadIdx.x >> 5); row < rows;
+       row += static_cast<int64_t>(gridDim.y) * kWarps) {
     const T* xr = x + row * ld;
     OnlineStat st{-INFINITY, 0.f, 0.f};
     if (vec_ok) {
-      constexpr int64_t kStride = static_cast<int64_t>(kRowThreads) * N;
-      int64_t c = c_begin + static_cast<int64_t>(threadIdx.x) * N;
+      constexpr int64_t kStride = 32 * N;
+      int64_t c = c_begin + static_cast<int64_t>(lane) * N;
       // two full vectors per step, both loads issued before the math (same element order as below)
       for (; c + kStride + N <= c_end; c += 2 * kStride) {
         float a[N], b[N];
@@ -143,22 +148,18 @@ __global__ void __launch_bounds__(kRowThreads)
         }
       }
     } else {
-      for (int64_t c = c_begin + threadIdx.x; c < c_end; c += kRowThreads) {
+      for (int64_t c = c_begin + lane; c < c_end; c += 32) {
         float v[1] = {V::scalar(xr + c)};
         online_add<1>(st, v, 1);
       }
     }
-    // warp merge, then across warps
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
       OnlineStat o{__shfl_xor_sync(0xffffffffu, st.m, off), __shfl_xor_sync(0xffffffffu, st.s, off),
                    __shfl_xor_sync(0xffffffffu, st.u, off)};
       online_merge(st, o);
     }
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = st;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      for (int w = 1; w < kRowThreads / 32; ++w) online_merge(st, red[w]);
+    if (lane == 0) {
       float zt = 0.f;
       if (target != nullptr) {
         const int64_t t = target[row];
@@ -166,7 +167,6 @@ __global__ void __launch_bounds__(kRowThreads)
       }
       partials[tile * tile_stride + row] = make_float4(st.m, st.s, st.u, zt);
     }
-    __syncthreads();
   }
 }
 
@@ -184,7 +184,8 @@ extern "C" int frx_logits_partials(const void* logits, int dtype, int64_t ld, in
               "frx_logits_partials: null logits/partials or unaligned partials");
   const int64_t n_tiles = (cols + tile_cols - 1) / tile_cols;
   FRX_REQUIRE(n_tiles < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_logits_partials: too many tiles");
-  const dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(rows < 65535 ? rows : 65535));
+  const int64_t row_blocks = (rows + kRowThreads / 32 - 1) / (kRowThreads / 32);
+  const dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(row_blocks < 65535 ? row_blocks : 65535));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == FRX_DTYPE_F32) {
     const int vec_ok = aligned16(logits) && ld % 4 == 0 && tile_cols % 4 == 0;

@@ -25,12 +25,14 @@ _TILE_COLS_MIN = 2048
 
 
 def _tile_cols(M: int, N: int) -> int:
-    # enough (row, tile) blocks to cover the GPU a few times; tiles a multiple of 8 columns
+    # one warp per (row, tile): enough of them to fill every SM (64 warps each) about twice over;
+    # tiles a multiple of 8 columns
     try:
         sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
     except Exception:
         sms = 148
-    want_tiles = max(1, (8 * sms + max(M, 1) - 1) // max(M, 1))
+    want_units = 2 * 64 * sms
+    want_tiles = max(1, (want_units + max(M, 1) - 1) // max(M, 1))
     tile = max(_TILE_COLS_MIN, (N + want_tiles - 1) // want_tiles)
     return (tile + 7) // 8 * 8
 

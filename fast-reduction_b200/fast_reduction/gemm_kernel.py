@@ -538,8 +538,10 @@ def _megakernel_fwd_bwd(hidden_2d, weight, target_1d, chunk_size, ce_weight, ent
 
 def _scale_grads(dloss: Tensor, *grads):
     # loss.backward() without an explicit gradient passes exactly 1.0: return the stored
-    # gradients without another full pass over them.
-    if dloss.numel() == 1 and float(dloss) == 1.0:
+    # gradients without another full pass over them. Reading dloss on the host synchronises, which
+    # a CUDA-graph capture forbids; while capturing, scale unconditionally (the reference's rule,
+    # gemm_kernel.py:909-915).
+    if dloss.numel() == 1 and not torch.cuda.is_current_stream_capturing() and float(dloss) == 1.0:
         return grads
     return tuple(None if g is None else g * dloss for g in grads)
 
