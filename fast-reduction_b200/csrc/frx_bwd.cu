@@ -38,6 +38,7 @@ struct StoreEpilogue {
     int cols;
     int out_f32;
     int out_f16;  // 16-bit output is fp16 (else bf16)
+    int accumulate;  // fp32 output: add the product to what the output holds
     int vec_ok;   // base and ld allow 16-byte vector stores
   };
 
@@ -61,12 +62,21 @@ struct StoreEpilogue {
         float* dst = static_cast<float*>(p.out) + off;
         if (lim >= 32 && p.vec_ok) {
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          for (int j = 0; j < 32; j += 4) {
+            float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if (p.accumulate) {
+              const float4 prev = *reinterpret_cast<const float4*>(dst + j);
+              o.x += prev.x;
+              o.y += prev.y;
+              o.z += prev.z;
+              o.w += prev.w;
+            }
+            *reinterpret_cast<float4*>(dst + j) = o;
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (j < lim) dst[j] = v[j];
+            if (j < lim) dst[j] = p.accumulate ? dst[j] + v[j] : v[j];
         }
       } else {
         const bool f16 = p.out_f16 != 0;
@@ -164,6 +174,9 @@ struct MultimemAddEpilogue {
 
 static int check_out(void* out, int64_t ld, int64_t cols, int out_dtype, const char* who) {
   FRX_REQUIRE(out != nullptr, FRX_ERR_INVALID_ARG, "%s: null output pointer", who);
+  FRX_REQUIRE((out_dtype & FRX_OUT_ACCUMULATE) == 0 || (out_dtype & ~FRX_OUT_ACCUMULATE) == FRX_DTYPE_F32,
+              FRX_ERR_INVALID_ARG, "%s: FRX_OUT_ACCUMULATE needs an fp32 output", who);
+  out_dtype &= ~FRX_OUT_ACCUMULATE;
   FRX_REQUIRE(out_dtype == FRX_DTYPE_BF16 || out_dtype == FRX_DTYPE_F16 || out_dtype == FRX_DTYPE_F32,
               FRX_ERR_INVALID_ARG, "%s: out_dtype must be FRX_DTYPE_BF16, FRX_DTYPE_F16 or FRX_DTYPE_F32", who);
   FRX_REQUIRE(ld >= cols, FRX_ERR_INVALID_ARG, "%s: output leading dimension %lld < %lld columns", who,
@@ -177,6 +190,8 @@ static StoreEpilogue::Params store_params(void* out, int64_t ld, int64_t rows, i
   ep.ld_out = ld;
   ep.rows = static_cast<int>(rows);
   ep.cols = static_cast<int>(cols);
+  ep.accumulate = (out_dtype & FRX_OUT_ACCUMULATE) ? 1 : 0;
+  out_dtype &= ~FRX_OUT_ACCUMULATE;
   ep.out_f32 = out_dtype == FRX_DTYPE_F32 ? 1 : 0;
   ep.out_f16 = out_dtype == FRX_DTYPE_F16 ? 1 : 0;
   const int64_t elem = ep.out_f32 ? 4 : 2;

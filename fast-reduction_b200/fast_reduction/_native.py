@@ -25,6 +25,11 @@ FRX_DTYPE_BF16 = 0
 FRX_DTYPE_F32 = 1
 FRX_DTYPE_F16 = 2
 
+FRX_OUT_ACCUMULATE = 256
+FRX_PART_HI = 0
+FRX_PART_MID = 1
+FRX_PART_LO = 2
+
 FRX_VOCAB_TILE = 256
 FRX_PARTIALS_REF_LAYOUT = 1
 FRX_IGNORE_NEGATIVE_TARGETS = 2
@@ -64,6 +69,7 @@ SIGNATURES: dict[str, tuple] = {
     "frx_logits_partials": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P]),
     "frx_column_sums": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _P]),
     "frx_gemm_dhidden_multicast": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I64, _I64, _I64, _P, _P]),
+    "frx_split_f32": (_I32, [_P, _I64, _I64, _I64, ctypes.c_uint32, _I32, _P, _I64, _I64, _P]),
 }
 
 _lib = None

@@ -76,9 +76,9 @@ def _input_device(*tensors: Optional[Tensor]) -> Optional[torch.device]:
 
 
 def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Optional[Tensor], allow_host: bool = False):
-    if hidden_states.dtype != weight.dtype or hidden_states.dtype not in (torch.bfloat16, torch.float16):
+    if hidden_states.dtype != weight.dtype or hidden_states.dtype not in (torch.bfloat16, torch.float16, torch.float32):
         raise NotImplementedError(
-            "the B200 engine computes in bf16 or fp16 (hidden and weight of the same type); got hidden "
+            "the B200 engine computes in bf16, fp16 or fp32 (hidden and weight of the same type); got hidden "
             f"{hidden_states.dtype}, weight {weight.dtype}"
         )
     if weight.dim() != 2:
@@ -86,7 +86,7 @@ def _prepare(hidden_states: Tensor, weight: Tensor, target: Tensor, bias: Option
     H = hidden_states.shape[-1]
     if weight.shape[1] != H:
         raise ValueError(f"hidden size mismatch: hidden [..., {H}] vs weight {tuple(weight.shape)}")
-    if H % 8 != 0:
+    if H % 8 != 0 and hidden_states.dtype != torch.float32:
         raise NotImplementedError(f"hidden size must be a multiple of 8 (TMA row alignment), got {H}")
     batch_shape = hidden_states.shape[:-1]
     hidden_2d = hidden_states.reshape(-1, H)
@@ -117,6 +117,46 @@ def _chunk_rows(chunk_size: int, B: int) -> int:
     if chunk_size is None or chunk_size <= 0:
         raise ValueError(f"chunk_size must be positive, got {chunk_size}")
     return max(1, min(int(chunk_size), B))
+
+
+def _fp32_k_operands(hidden_2d: Tensor, weight: Tensor, bias: Optional[Tensor]) -> Tuple[Tensor, Tensor]:
+    """bf16 operands whose product is the fp32 product hidden @ weight.T (+ bias), for the forward GEMM.
+
+    bf16x6 (Henry, Tang, Heinecke, ARITH 2019): each fp32 matrix is split into bf16 hi / mid / lo parts
+    (frx_split_f32) and six parts of each are concatenated along K, so one bf16 GEMM with K = 6 H sums
+    hi.hi + hi.mid + mid.hi + hi.lo + lo.hi + mid.mid in fp32 TMEM. A bias rides along as three more
+    K columns (ones against its own hi / mid / lo). K is zero-padded to a multiple of 8."""
+    B, H = hidden_2d.shape
+    V = weight.shape[0]
+    dev = hidden_2d.device
+    n = len(ops.SPLIT_LEFT)
+    extra = 3 if bias is not None else 0
+    K = ops.round_up(n * H + extra, 8)
+    x6 = torch.empty(B, K, device=dev, dtype=torch.bfloat16)
+    w6 = torch.empty(V, K, device=dev, dtype=torch.bfloat16)
+    x6[:, n * H:].zero_()
+    w6[:, n * H:].zero_()
+    if B:
+        ops.split_f32(hidden_2d, x6, ops.SPLIT_LEFT, part_stride=H)
+    ops.split_f32(weight, w6, ops.SPLIT_RIGHT, part_stride=H)
+    if bias is not None:
+        x6[:, n * H:n * H + 3] = 1.0
+        ops.split_f32(bias.view(V, 1), w6[:, n * H:], (_HI, _MID, _LO), part_stride=1)
+    return x6, w6
+
+
+_HI, _MID, _LO = 0, 1, 2
+
+
+def _fp32_parts(x: Tensor) -> Tensor:
+    """[3, rows, cols] bf16 views (row stride a multiple of 8 elements, as TMA wants): the hi / mid /
+    lo parts of the fp32 matrix x [rows, cols]."""
+    rows, cols = x.shape
+    ld = ops.round_up(max(cols, 1), 8)
+    out = torch.empty(3, rows, ld, device=x.device, dtype=torch.bfloat16)
+    if rows and cols:
+        ops.split_f32(x, out[0], (_HI, _MID, _LO), part_stride=rows * ld)
+    return out[:, :, :cols]
 
 
 def forward_stats(
@@ -304,6 +344,11 @@ def gemm_fused_ce_entropy(
     batch_shape, hidden_2d, weight, target_1d, bias = _prepare(hidden_states, weight, target, bias,
                                                                allow_host=True)
     dev = _input_device(hidden_2d, weight, target_1d, bias)
+    if dev is not None and hidden_2d.dtype == torch.float32:
+        # fp32 operands are split on the device before the GEMM: upload them whole, then run there
+        moved = [None if t is None else t.to(dev, non_blocking=True) for t in (hidden_2d, weight, target_1d, bias)]
+        res = gemm_fused_ce_entropy(*moved, chunk_size=chunk_size, ignore_index=ignore_index)
+        return _results_to(hidden_states.device, batch_shape, *res)
     if dev is not None:
         B = hidden_2d.shape[0]
         ce, ent, logp = (torch.empty(B, device=dev, dtype=torch.float32) for _ in range(3))
@@ -315,6 +360,9 @@ def gemm_fused_ce_entropy(
     ce = torch.empty(B, device=dev, dtype=torch.float32)
     ent = torch.empty(B, device=dev, dtype=torch.float32)
     logp = torch.empty(B, device=dev, dtype=torch.float32)
+    if hidden_2d.dtype == torch.float32:
+        hidden_2d, weight = _fp32_k_operands(hidden_2d, weight, bias)
+        bias = None
     forward_stats(hidden_2d, weight, target_1d, chunk_size, ce=ce, entropy=ent, log_probs=logp,
                   ignore_index=ignore_index, bias=bias)
     return ce.view(batch_shape), ent.view(batch_shape), logp.view(batch_shape)
@@ -353,8 +401,13 @@ class GemmFusedCEEntropy(torch.autograd.Function):
         ent = torch.empty(B, device=dev, dtype=torch.float32)
         lse = torch.empty(B, device=dev, dtype=torch.float32)
         logp = torch.empty(B, device=dev, dtype=torch.float32)
-        forward_stats(hidden_2d, weight_c, target_1d, chunk_size, ce=ce, entropy=ent, lse=lse, log_probs=logp,
-                      bias=bias_c)
+        if hidden_2d.dtype == torch.float32:
+            x_fwd, w_fwd = _fp32_k_operands(hidden_2d, weight_c, bias_c)
+            forward_stats(x_fwd, w_fwd, target_1d, chunk_size, ce=ce, entropy=ent, lse=lse, log_probs=logp)
+            del x_fwd, w_fwd
+        else:
+            forward_stats(hidden_2d, weight_c, target_1d, chunk_size, ce=ce, entropy=ent, lse=lse, log_probs=logp,
+                          bias=bias_c)
         ctx.save_for_backward(hidden_2d, weight_c, target_1d, lse, ent, bias_c)
         ctx.chunk_size = chunk_size
         ctx.hidden_shape = hidden_states.shape
@@ -429,9 +482,10 @@ def fwd_bwd_shard(
     d_bias [V_shard] or None, pending).
 
     By default d_hidden is this shard's [B, H] contribution in the hidden dtype and pending is None.
-    A ``dhidden_fn(dz)`` replaces that step (it runs between the dlogits pass and the d_weight GEMM,
+    A ``dhidden_fn(pairs)`` replaces that step (it runs between the dlogits pass and the d_weight GEMM,
     so a cross-shard reduction it starts overlaps the d_weight GEMM) and its (d_hidden, pending) pair
-    is returned instead.
+    is returned instead; ``pairs`` lists the (dlogits, weight) operand pairs whose frx_gemm_dhidden
+    products sum to the contribution (one pair, or six bf16x6 pairs for fp32 operands).
 
     For each row chunk: GEMM epilogue writes the chunk's fp32 logits (and partials); the
     per-row lse / entropy of the chunk are produced by ``stats_fn(start, end, partials, T, chunk)``
@@ -453,7 +507,20 @@ def fwd_bwd_shard(
     n_buf = 2 if overlap else 1
     logits_bufs = [torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32) for _ in range(n_buf)]
     partials_bufs = [torch.empty(T, chunk, 4, device=dev, dtype=torch.float32) for _ in range(n_buf)]
-    dz = torch.empty(B, ops.round_up(V, 8), device=dev, dtype=hidden_2d.dtype)
+    ldz = ops.round_up(V, 8)
+    f32 = hidden_2d.dtype == torch.float32
+    if f32:
+        # fp32 operands (the reference's fp32 matmul): the forward GEMM runs on bf16x6 K-concatenated
+        # operands (bias folded in), the fp32 dlogits are split into hi / mid / lo parts, and each
+        # backward product is the sum of six bf16 GEMMs accumulated in an fp32 output.
+        x_fwd, w_fwd = _fp32_k_operands(hidden_2d, weight, bias)
+        fwd_bias = None
+        dz_parts = torch.empty(3, B, ldz, device=dev, dtype=torch.bfloat16)
+        dz32 = torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32)
+        dz = None
+    else:
+        x_fwd, w_fwd, fwd_bias = hidden_2d, weight, bias
+        dz = torch.empty(B, ldz, device=dev, dtype=hidden_2d.dtype)
     main = torch.cuda.current_stream(dev)
     side = _side_stream(dev) if overlap else None
     if side is not None:
@@ -466,18 +533,21 @@ def fwd_bwd_shard(
         logits, partials = logits_bufs[buf], partials_bufs[buf]
         if done[buf] is not None:
             main.wait_event(done[buf])
-        ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
-                         logits=logits, bias=bias)
+        ops.fwd_partials(x_fwd[start:end], w_fwd, target_1d[start:end], partials, chunk, vocab_offset,
+                         logits=logits, bias=fwd_bias)
 
         def run_dlogits(logits=logits, partials=partials, start=start, end=end, rows=rows):
             stats_fn(start, end, partials, T, chunk)
             ops.dlogits(
-                logits, target_1d[start:end], lse[start:end], entropy[start:end], dz[start:end],
+                logits, target_1d[start:end], lse[start:end], entropy[start:end],
+                dz32 if f32 else dz[start:end],
                 rows=rows, vocab_shard=V, ce_weight=ce_weight, ent_weight=ent_weight,
                 g_ce=None if g_ce is None else g_ce[start:end],
                 g_ent=None if g_ent is None else g_ent[start:end],
                 vocab_offset=vocab_offset, ignore_index=ignore_index,
             )
+            if f32:
+                ops.split_f32(dz32[:rows, :V], dz_parts[0, start:end], (_HI, _MID, _LO), part_stride=B * ldz)
 
         if side is None:
             run_dlogits()
@@ -492,22 +562,44 @@ def fwd_bwd_shard(
             done[buf] = ev
     if side is not None:
         main.wait_stream(side)
-        for t_ in logits_bufs + partials_bufs + [dz, lse, entropy, target_1d, g_ce, g_ent]:
+        for t_ in logits_bufs + partials_bufs + [dz, lse, entropy, target_1d, g_ce, g_ent] + (
+                [dz32, dz_parts] if f32 else []):
             if t_ is not None:
                 t_.record_stream(side)
     del logits_bufs, partials_bufs, partials
+    if f32:
+        del x_fwd, w_fwd, dz32
+        w_parts = _fp32_parts(weight)
+        dh_pairs = [(dz_parts[i], w_parts[j]) for i, j in zip(ops.SPLIT_LEFT, ops.SPLIT_RIGHT)]
+    else:
+        dh_pairs = [(dz, weight)]
     if dhidden_fn is not None:
-        d_hidden, pending = dhidden_fn(dz)
+        d_hidden, pending = dhidden_fn(dh_pairs)
     else:
         d_hidden = torch.empty(B, H, device=dev, dtype=hidden_2d.dtype)
-        ops.gemm_dhidden(dz, weight, d_hidden, rows=B, vocab_shard=V)
+        for i, (a_op, b_op) in enumerate(dh_pairs):
+            ops.gemm_dhidden(a_op, b_op, d_hidden, rows=B, vocab_shard=V, accumulate=i > 0)
         pending = None
     d_weight = torch.empty(V, H, device=dev, dtype=weight.dtype)
-    ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
+    if f32:
+        del w_parts, dh_pairs
+        x_parts = _fp32_parts(hidden_2d)
+        for n_, (i, j) in enumerate(zip(ops.SPLIT_LEFT, ops.SPLIT_RIGHT)):
+            ops.gemm_dweight(dz_parts[i], x_parts[j], d_weight, rows=B, vocab_shard=V, accumulate=n_ > 0)
+    else:
+        ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
     d_bias = None
     if bias is not None:
         d_bias32 = torch.empty(V, device=dev, dtype=torch.float32)
-        ops.column_sums(dz, d_bias32, rows=B, cols=V)
+        if f32:
+            # the parts' column sums, added in a fixed order (hi + mid + lo = the fp32 dlogits)
+            sums = torch.empty(3, V, device=dev, dtype=torch.float32)
+            for i in range(3):
+                ops.column_sums(dz_parts[i], sums[i], rows=B, cols=V)
+            torch.add(sums[0], sums[1], out=d_bias32)
+            d_bias32.add_(sums[2])
+        else:
+            ops.column_sums(dz, d_bias32, rows=B, cols=V)
         d_bias = d_bias32.to(bias.dtype)
     return d_hidden, d_weight, d_bias, pending
 

@@ -203,14 +203,44 @@ def dlogits(
     nat.check(rc, "frx_dlogits")
 
 
-def _out_dtype(t: torch.Tensor) -> int:
+def _out_dtype(t: torch.Tensor, accumulate: bool = False) -> int:
     if t.dtype not in _OUT_DTYPES:
         raise TypeError("GEMM output must be bfloat16, float16 or float32")
+    if accumulate:
+        if t.dtype != torch.float32:
+            raise TypeError("accumulating GEMM output must be float32")
+        return _OUT_DTYPES[t.dtype] | nat.FRX_OUT_ACCUMULATE
     return _OUT_DTYPES[t.dtype]
 
 
-def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int) -> None:
-    """out[rows, H] <- dz[rows, vocab_shard] @ weight[vocab_shard, H]."""
+# bf16x6 emulation of an fp32 product (Henry, Tang, Heinecke, ARITH 2019): the left operand's parts
+# in this order times the right operand's parts in the other order sum to the product up to the
+# mid*lo, lo*mid and lo*lo terms.
+SPLIT_LEFT = (nat.FRX_PART_HI, nat.FRX_PART_HI, nat.FRX_PART_MID, nat.FRX_PART_HI, nat.FRX_PART_LO, nat.FRX_PART_MID)
+SPLIT_RIGHT = (nat.FRX_PART_HI, nat.FRX_PART_MID, nat.FRX_PART_HI, nat.FRX_PART_LO, nat.FRX_PART_HI, nat.FRX_PART_MID)
+
+
+def split_f32(x: torch.Tensor, out: torch.Tensor, parts, *, part_stride: int) -> None:
+    """out (bf16, row stride out.stride(0)) + p * part_stride <- part parts[p] (hi / mid / lo) of the
+    fp32 matrix x [rows, cols]: x = hi + mid + lo to ~24 bits (frx_split_f32)."""
+    dev = _require_cuda(x, out)
+    if x.dtype != torch.float32 or out.dtype != torch.bfloat16:
+        raise TypeError("split_f32 takes a float32 matrix and writes bfloat16 parts")
+    ldx = _row_major(x, "x")
+    ldo = _row_major(out, "out")
+    rows, cols = x.shape
+    code = 0
+    for p, sel in enumerate(parts):
+        code |= int(sel) << (2 * p)
+    lib = nat.load()
+    rc = _launch("split_f32", dev, lambda: lib.frx_split_f32(
+        x.data_ptr(), ldx, rows, cols, code, len(parts), out.data_ptr(), ldo, part_stride, nat.stream_of(dev)))
+    nat.check(rc, "frx_split_f32")
+
+
+def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int,
+                 accumulate: bool = False) -> None:
+    """out[rows, H] <- dz[rows, vocab_shard] @ weight[vocab_shard, H] (``accumulate``: fp32 out +=)."""
     dev = _require_cuda(dz, weight, out)
     dt = _gemm_dtype(dz, weight)
     ldz = _row_major(dz, "dz")
@@ -221,15 +251,16 @@ def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, r
         raise ValueError("shape mismatch in gemm_dhidden")
     lib = nat.load()
     rc = _launch("gemm_dhidden", dev, lambda: lib.frx_gemm_dhidden(
-        dz.data_ptr(), ldz, weight.data_ptr(), ldw, dt, out.data_ptr(), ldo, _out_dtype(out), rows, hdim,
+        dz.data_ptr(), ldz, weight.data_ptr(), ldw, dt, out.data_ptr(), ldo, _out_dtype(out, accumulate), rows, hdim,
         vocab_shard,
         nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_gemm_dhidden")
 
 
-def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int) -> None:
-    """out[vocab_shard, H] <- dz[rows, vocab_shard]^T @ hidden[rows, H]."""
+def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int,
+                 accumulate: bool = False) -> None:
+    """out[vocab_shard, H] <- dz[rows, vocab_shard]^T @ hidden[rows, H] (``accumulate``: fp32 out +=)."""
     dev = _require_cuda(dz, hidden, out)
     dt = _gemm_dtype(dz, hidden)
     ldz = _row_major(dz, "dz")
@@ -240,7 +271,8 @@ def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, r
         raise ValueError("shape mismatch in gemm_dweight")
     lib = nat.load()
     rc = _launch("gemm_dweight", dev, lambda: lib.frx_gemm_dweight(
-        dz.data_ptr(), ldz, hidden.data_ptr(), ldh, dt, out.data_ptr(), ldo, _out_dtype(out), vocab_shard, hdim, rows,
+        dz.data_ptr(), ldz, hidden.data_ptr(), ldh, dt, out.data_ptr(), ldo, _out_dtype(out, accumulate), vocab_shard,
+        hdim, rows,
         nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_gemm_dweight")

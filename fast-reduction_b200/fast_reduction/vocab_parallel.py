@@ -106,7 +106,16 @@ def vocab_parallel_ce_entropy(
     host_dev = gk._input_device(hidden_2d, weight_shard, target_1d, bias_shard)
     dev = hidden_2d.device if host_dev is None else host_dev
     local = torch.empty(B, 4, device=dev, dtype=torch.float32)
+    if host_dev is not None and hidden_2d.dtype == torch.float32:
+        # fp32 operands are split on the device before the GEMM: upload them whole first
+        hidden_2d, weight_shard, target_1d, bias_shard = (
+            None if t is None else t.to(host_dev, non_blocking=True)
+            for t in (hidden_2d, weight_shard, target_1d, bias_shard))
+        host_dev = None
     if host_dev is None:
+        if hidden_2d.dtype == torch.float32:
+            hidden_2d, weight_shard = gk._fp32_k_operands(hidden_2d, weight_shard, bias_shard)
+            bias_shard = None
         gk.forward_stats(hidden_2d, weight_shard, target_1d, chunk_size, vocab_offset=vocab_start, merged=local,
                          vocab_size=vocab_size, ignore_index=ignore_index, bias=bias_shard)
         t_d = target_1d
@@ -154,13 +163,15 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
         # rank's d_hidden GEMM starts adding into the buffers.
         buf.zero_()
 
-        def dhidden_fn(dz):
-            ops.gemm_dhidden_multicast(dz, weight_shard, hdl.multicast_ptr, H, rows=B, vocab_shard=Vr, device=dev)
+        def dhidden_fn(pairs):
+            for a_op, b_op in pairs:  # multimem.red adds every product into every rank's copy
+                ops.gemm_dhidden_multicast(a_op, b_op, hdl.multicast_ptr, H, rows=B, vocab_shard=Vr, device=dev)
             return None, None
     else:
-        def dhidden_fn(dz):
+        def dhidden_fn(pairs):
             dh = torch.empty(B, H, device=dev, dtype=torch.float32)
-            ops.gemm_dhidden(dz, weight_shard, dh, rows=B, vocab_shard=Vr)
+            for i, (a_op, b_op) in enumerate(pairs):
+                ops.gemm_dhidden(a_op, b_op, dh, rows=B, vocab_shard=Vr, accumulate=i > 0)
             return dh, _allreduce_async(dh, group)
 
     d_hidden_f32, d_weight, d_bias, pending = gk.fwd_bwd_shard(

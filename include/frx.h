@@ -49,6 +49,15 @@ extern "C" {
 #define FRX_DTYPE_F32 1
 #define FRX_DTYPE_F16 2
 
+/* Or-ed into the out_dtype of frx_gemm_dhidden / frx_gemm_dweight with FRX_DTYPE_F32: the product is
+ * added to the fp32 values the output already holds (several launches accumulate one result). */
+#define FRX_OUT_ACCUMULATE 256
+
+/* frx_split_f32 part selectors (2 bits per part, part p at bits [2p, 2p+2)) */
+#define FRX_PART_HI 0
+#define FRX_PART_MID 1
+#define FRX_PART_LO 2
+
 /* Width of one vocabulary tile of the forward partials (columns per partial). */
 #define FRX_VOCAB_TILE 256
 
@@ -124,7 +133,8 @@ FRX_API int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t* t
 /*
  * d_hidden[rows, hidden_dim] = dlogits[rows, vocab_shard] @ weight[vocab_shard, hidden_dim]
  * (in_dtype = FRX_DTYPE_BF16 or _F16 for both inputs, fp32 accumulation, out_dtype out: BF16, F16
- * or F32). Replaces the cuBLAS `torch.mm(dlogits, weight)` of the reference's megakernel
+ * or F32, or F32 | FRX_OUT_ACCUMULATE to add into the output). Replaces the cuBLAS
+ * `torch.mm(dlogits, weight)` of the reference's megakernel
  * (fast_reduction/gemm_kernel.py:859-862).
  */
 FRX_API int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void* weight, int64_t ld_weight,
@@ -149,13 +159,28 @@ FRX_API int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogits, 
 /*
  * d_weight[vocab_shard, hidden_dim] = dlogits[rows, vocab_shard]^T @ hidden[rows, hidden_dim]
  * (in_dtype = FRX_DTYPE_BF16 or _F16 for both inputs) accumulated over all `rows` in fp32 tensor
- * memory and written once in out_dtype (BF16, F16 or F32). Replaces
+ * memory and written once in out_dtype (BF16, F16 or F32, or F32 | FRX_OUT_ACCUMULATE). Replaces
  * the per-chunk `d_weight.add_(torch.mm(dlogits.t(), h_chunk).float())` and the final cast
  * of the reference (fast_reduction/gemm_kernel.py:864-871).
  */
 FRX_API int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
                      int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
                      int64_t hidden_dim, int64_t rows, int* status, void* stream);
+
+/*
+ * Splits an fp32 matrix x [rows, cols] (row stride ld_x) into bf16 parts for the bf16x6 emulation of
+ * an fp32 matrix product on the bf16 tensor cores (Henry, Tang, Heinecke, "Leveraging the bfloat16
+ * Artificial Intelligence Datatype For Higher-Precision Computations", ARITH 2019):
+ *   hi = bf16(x),  mid = bf16(x - hi),  lo = bf16(x - hi - mid)   (x = hi + mid + lo to ~24 bits).
+ * For p < n_parts, part p (FRX_PART_HI / _MID / _LO, selected by bits [2p, 2p+2) of `parts`) is
+ * written to out + p * part_stride as a [rows, cols] bf16 matrix with row stride ld_out. With the left
+ * operand split as (hi, hi, mid, hi, lo, mid) and the right as (hi, mid, hi, lo, hi, mid), the six
+ * products sum to x.y up to the dropped mid*lo, lo*mid and lo*lo terms (~2^-24 relative): an fp32
+ * product. Replaces the fp32 matmul the reference runs for fp32 inputs (fast_reduction/kernel.py:32-45
+ * `_mm_setup`; gemm_kernel.py:859-866).
+ */
+FRX_API int frx_split_f32(const float* x, int64_t ld_x, int64_t rows, int64_t cols, uint32_t parts, int n_parts,
+                          void* out, int64_t ld_out, int64_t part_stride, void* stream);
 
 /*
  * Column sums out[c] = sum_r x[r, c] (fp32 accumulation, fixed order, so deterministic) of a bf16 or

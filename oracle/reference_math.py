@@ -287,3 +287,31 @@ def make_inputs(B: int, H: int, V: int, seed: int = 0, weight_std: Optional[floa
         idx = torch.randperm(B, generator=g)[:n]
         target[idx] = IGNORE_INDEX
     return hidden, weight, target
+
+
+def split_bf16x3(x: torch.Tensor):
+    """(hi, mid, lo) bf16 parts of an fp32 tensor with x = hi + mid + lo to ~24 bits: the split of the
+    bf16x6 emulation of fp32 products (Henry, Tang, Heinecke, "Leveraging the bfloat16 Artificial
+    Intelligence Datatype For Higher-Precision Computations", ARITH 2019). Each residual is exact in
+    fp32. Restates what frx_split_f32 computes, for the CPU checks of the method."""
+    x = x.float()
+    hi = x.to(torch.bfloat16)
+    r1 = x - hi.float()
+    mid = r1.to(torch.bfloat16)
+    r2 = r1 - mid.float()
+    lo = r2.to(torch.bfloat16)
+    return hi, mid, lo
+
+
+# Part pairs whose products the bf16x6 scheme keeps: (left part, right part), 0 = hi, 1 = mid, 2 = lo.
+BF16X6_PAIRS = ((0, 0), (0, 1), (1, 0), (0, 2), (2, 0), (1, 1))
+
+
+def bf16x6_matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a @ b from the six bf16 part products (each exact in fp64 here), the arithmetic the GPU path
+    performs with fp32 accumulation."""
+    pa, pb = split_bf16x3(a), split_bf16x3(b)
+    out = torch.zeros(a.shape[0], b.shape[1], dtype=torch.float64)
+    for i, j in BF16X6_PAIRS:
+        out += pa[i].double() @ pb[j].double()
+    return out

@@ -51,7 +51,7 @@ def test_constants_match_header():
                  "FRX_DTYPE_F32", "FRX_DTYPE_F16", "FRX_VOCAB_TILE", "FRX_PARTIALS_REF_LAYOUT",
                  "FRX_IGNORE_NEGATIVE_TARGETS", "FRX_STATUS_BAD_TARGET",
                  "FRX_STATUS_TIMEOUT_PRODUCER", "FRX_STATUS_TIMEOUT_MMA", "FRX_STATUS_TIMEOUT_EPILOGUE",
-                 "FRX_STATUS_DRAIN_TIMEOUT"):
+                 "FRX_STATUS_DRAIN_TIMEOUT", "FRX_OUT_ACCUMULATE", "FRX_PART_HI", "FRX_PART_MID", "FRX_PART_LO"):
         val = int(re.search(rf"#define {name} (\d+)", hdr).group(1))
         assert getattr(nat, name) == val, name
 
@@ -84,6 +84,13 @@ def test_invalid_arguments_return_codes_without_gpu():
     assert rc == nat.FRX_ERR_INVALID_ARG  # column sums read 16-bit matrices only
     rc = lib.frx_dlogits(1 << 20, 8, None, 1 << 21, 1 << 21, None, None, 1.0, -1.0, 1 << 22, 8, 9, 4, 4, 0, 0, None)
     assert rc == nat.FRX_ERR_INVALID_ARG  # unknown out_dtype
+    rc = lib.frx_gemm_dhidden(1 << 20, 64, 1 << 21, 64, 0, 1 << 22, 64, nat.FRX_DTYPE_BF16 | nat.FRX_OUT_ACCUMULATE,
+                              64, 64, 64, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # accumulation needs an fp32 output
+    assert b"FRX_OUT_ACCUMULATE" in lib.frx_last_error()
+    rc = lib.frx_split_f32(1 << 20, 8, 4, 8, 3, 1, 1 << 21, 8, 32, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # part selector 3 does not exist
+    assert lib.frx_split_f32(None, 8, 0, 8, 0, 1, None, 8, 0, None) == nat.FRX_OK  # empty
 
 
 def test_empty_problems_are_noops():

@@ -44,8 +44,8 @@ def test_bias_checks():
 
 
 def test_unsupported_dtypes_rejected():
-    h, w, t = _inputs(dtype=torch.float32)
-    with pytest.raises(NotImplementedError, match="bf16 or fp16"):
+    h, w, t = _inputs(dtype=torch.float64)
+    with pytest.raises(NotImplementedError, match="bf16, fp16 or fp32"):
         gk.gemm_fused_ce_entropy(h, w, t)
     h, w, t = _inputs()
     with pytest.raises(NotImplementedError, match="same type"):

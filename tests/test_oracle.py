@@ -179,3 +179,22 @@ def test_bias_restatement_matches_reference_autograd():
         np.testing.assert_allclose(got.numpy(), g[key], rtol=1e-5, atol=1e-6)
     ce2, ent2, _, _ = rm.fp32_reference(h, w, t, bias=b)
     np.testing.assert_allclose(ce2.numpy(), g["bias_ce"], rtol=1e-5, atol=1e-6)
+
+
+def test_bf16x6_split_is_exact_and_product_is_fp32_accurate():
+    """The fp32 input path's arithmetic (bf16x6, Henry et al. 2019) on the CPU: hi + mid + lo
+    reproduces x, and the six kept part products give a @ b to fp32 accuracy."""
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(64, 96, generator=g) * torch.logspace(-20, 20, 96).float()
+    hi, mid, lo = rm.split_bf16x3(x)
+    rec = hi.double() + mid.double() + lo.double()
+    rel = ((rec - x.double()).abs() / x.double().abs().clamp_min(1e-30)).max()
+    assert rel < 2 ** -22, float(rel)
+    a = torch.randn(50, 300, generator=g)
+    b = torch.randn(300, 70, generator=g)
+    exact = a.double() @ b.double()
+    emu = rm.bf16x6_matmul(a, b)
+    scale = (a.double().abs() @ b.double().abs())
+    assert ((emu - exact).abs() / scale).max() < 2 ** -21
+    one_pass = a.to(torch.bfloat16).double() @ b.to(torch.bfloat16).double()
+    assert ((one_pass - exact).abs() / scale).max() > 2 ** -12  # what a plain bf16 product would lose
