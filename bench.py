@@ -232,10 +232,44 @@ def cpu_baseline(B, H, V, chunk, budget_s: float = 12.0) -> dict:
     rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
     el = time.perf_counter() - t0
     ms_full = el * 1000.0 * B / rows
+
+    # training step (the chunked autograd loop of the reference's benchmarks/bench_fwd_bwd.py:177-195)
+    # on a smaller row sample, extrapolated the same way
+    rows_fb = max(64, rows // 4 // 64 * 64)
+    hf = h[:rows_fb]
+    t0 = time.perf_counter()
+    rm.chunked_fwd_bwd(hf, weight, t[:rows_fb], chunk_size=chunk)
+    el_fb = time.perf_counter() - t0
+    del hf
+
+    # configs[0] (B=1024, H=1024, V=32000, chunk 512), timed whole after one warm-up call
+    g0 = torch.Generator().manual_seed(0)
+    h0 = torch.randn(1024, 1024, generator=g0).to(torch.bfloat16)
+    w0 = (torch.randn(32000, 1024, generator=g0) / math.sqrt(1024)).to(torch.bfloat16)
+    t0_ = torch.randint(0, 32000, (1024,), generator=g0)
+    rm.chunked_linear_xent_entropy(h0, w0, t0_, chunk_size=512)
+    t0 = time.perf_counter()
+    rm.chunked_linear_xent_entropy(h0, w0, t0_, chunk_size=512)
+    el0 = time.perf_counter() - t0
     return {"value": round(ms_full, 1), "unit": "ms", "cores": threads, "kind": "port",
             "sample": f"{rows} of {B} rows (full V={V}, H={H}) in {el:.1f} s on {threads} threads, "
                       f"extrapolated linearly to B={B}; oracle/reference_math.chunked_linear_xent_entropy "
-                      f"(restates reference baseline.py:207-241), torch CPU bf16 matmul"}
+                      f"(restates reference baseline.py:207-241), torch CPU bf16 matmul",
+            "fwd_bwd_ms": round(el_fb * 1000.0 * B / rows_fb, 1),
+            "fwd_bwd_sample": f"{rows_fb} of {B} rows in {el_fb:.1f} s, extrapolated linearly; "
+                              f"oracle/reference_math.chunked_fwd_bwd (restates benchmarks/bench_fwd_bwd.py:177-195)",
+            "config0_fwd_ms": round(el0 * 1000.0, 1),
+            "cpu_model": _cpu_model(), "os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads()}
+
+
+def _cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def run_reference(args, world, rank):
