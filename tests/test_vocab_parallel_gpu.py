@@ -17,7 +17,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q, nvls):
+def _worker(rank, world, port, q, nvls, dtype_name="bfloat16"):
     try:
         import datetime
         import os
@@ -41,8 +41,10 @@ def _worker(rank, world, port, q, nvls):
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=dev)
         B, H, V, chunk = 520, 256, 3001, 200
+        dtype = getattr(torch, dtype_name)
         h, w, t = rm.make_inputs(B, H, V, seed=5, weight_std=0.1, ignore_frac=0.05, tail_frac=0.02)
-        bias = (torch.randn(V, generator=torch.Generator().manual_seed(9)) * 0.5).to(torch.bfloat16)
+        h, w = h.to(dtype), w.to(dtype)
+        bias = (torch.randn(V, generator=torch.Generator().manual_seed(9)) * 0.5).to(dtype)
         a, b = shard_bounds(V, world, rank)
         hd, td = h.to(dev), t.to(dev)
         ce, ent, lp = vocab_parallel_ce_entropy(hd, w[a:b].to(dev), td, a, V, chunk_size=chunk,
@@ -80,15 +82,18 @@ def _worker(rank, world, port, q, nvls):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least two GPUs")
-@pytest.mark.parametrize("nvls", [True, False], ids=["nvls-fused-dhidden", "nccl-allreduce"])
-def test_vocab_parallel_matches_single_gpu(nvls):
+@pytest.mark.parametrize("nvls,dtype_name", [(True, "bfloat16"), (False, "bfloat16"), (False, "float16"),
+                                             (False, "float32")],
+                         ids=["nvls-fused-dhidden", "nccl-allreduce", "nccl-fp16", "nccl-fp32"])
+def test_vocab_parallel_matches_single_gpu(nvls, dtype_name):
     """Both d_hidden reductions: the NCCL all-reduce (default) and the reduction fused into the GEMM
-    through NVLS multicast (FRX_NVLS=1; when the GPUs lack NVLS this case runs the NCCL path too)."""
+    through NVLS multicast (FRX_NVLS=1; when the GPUs lack NVLS this case runs the NCCL path too);
+    fp16 and fp32 operands on the default path."""
     world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, nvls)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, nvls, dtype_name)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
