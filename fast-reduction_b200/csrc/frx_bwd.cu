@@ -202,8 +202,8 @@ static StoreEpilogue::Params store_params(void* out, int64_t ld, int64_t rows, i
 }  // namespace frx
 
 extern "C" int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const void* weight, int64_t ld_weight,
-                                int in_dtype, void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows, int64_t hidden_dim,
-                                int64_t vocab_shard, int* status, void* stream) {
+                                int in_dtype, void* d_hidden, int64_t ld_d_hidden, int out_dtype, int64_t rows,
+                                int64_t hidden_dim, int64_t vocab_shard, int* status, void* stream) {
   using namespace frx;
   FRX_REQUIRE(rows >= 0 && hidden_dim >= 1 && vocab_shard >= 1 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
                   vocab_shard < (1ll << 31),

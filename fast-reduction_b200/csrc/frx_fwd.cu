@@ -183,12 +183,13 @@ struct CEPartialsEpilogue {
 
 }  // namespace frx
 
-extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
-                                int dtype, const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
-                                int64_t hidden_dim,
-                                int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
-                                int64_t ld_logits, int* status, void* stream) {
-  using namespace frx;
+namespace frx {
+
+static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight, int dtype,
+                             const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
+                             int64_t hidden_dim, int64_t vocab_offset, float* partials, int64_t tile_stride,
+                             float* logits, int64_t ld_logits, int* status, void* stream, int stall_kb,
+                             uint64_t wait_limit_ns) {
   FRX_REQUIRE(rows >= 0 && vocab_shard >= 1 && hidden_dim >= 1, FRX_ERR_INVALID_ARG,
               "frx_fwd_partials: bad sizes rows=%lld vocab_shard=%lld hidden_dim=%lld", (long long)rows,
               (long long)vocab_shard, (long long)hidden_dim);
@@ -231,5 +232,32 @@ extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const voi
   // A band of up to 64 row blocks (8192 rows, 64 MiB of bf16 hidden at H=4096) stays in L2
   // while the CTAs sweep the vocabulary.
   return launch_gemm<false, false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, 64, ep, status,
-                                                       static_cast<cudaStream_t>(stream));
+                                                              static_cast<cudaStream_t>(stream), stall_kb,
+                                                              wait_limit_ns);
+}
+
+}  // namespace frx
+
+extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
+                                int dtype, const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
+                                int64_t hidden_dim, int64_t vocab_offset, float* partials, int64_t tile_stride,
+                                float* logits, int64_t ld_logits, int* status, void* stream) {
+  return frx::fwd_partials_impl(hidden, ld_hidden, weight, ld_weight, dtype, bias, target, rows, vocab_shard,
+                                hidden_dim, vocab_offset, partials, tile_stride, logits, ld_logits, status, stream, -1,
+                                frx::kWaitLimitNs);
+}
+
+extern "C" int frx_test_stalled_fwd(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
+                                    const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
+                                    float* partials, int64_t tile_stride, int stall_kb, int64_t wait_limit_us,
+                                    int* status, void* stream) {
+  using namespace frx;
+  FRX_REQUIRE(stall_kb >= 0 && wait_limit_us >= 1 && wait_limit_us <= 1000000, FRX_ERR_INVALID_ARG,
+              "frx_test_stalled_fwd: need stall_kb >= 0 and 1 <= wait_limit_us <= 1e6");
+  FRX_REQUIRE(stall_kb * 128 < hidden_dim, FRX_ERR_INVALID_ARG,
+              "frx_test_stalled_fwd: stall_kb %d is past the last k-block of hidden_dim %lld", stall_kb,
+              (long long)hidden_dim);
+  return fwd_partials_impl(hidden, ld_hidden, weight, ld_weight, FRX_DTYPE_BF16, nullptr, target, rows, vocab_shard,
+                           hidden_dim, 0, partials, tile_stride, nullptr, 0, status, stream, stall_kb,
+                           static_cast<uint64_t>(wait_limit_us) * 1000ull);
 }

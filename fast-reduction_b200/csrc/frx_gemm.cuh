@@ -49,6 +49,11 @@ struct TileSched {
   int num_tiles;
   int n256;  // number of 256-column blocks of the output (epilogue bound for wide tiles)
   int f16;   // operands are fp16 (else bf16)
+  // Failure-detection testing only: when >= 0, the producer of the (leading) CTA leaves k-block
+  // stall_kb of its first tile unfilled (no expect-tx, no copies), so the MMA warp's bounded wait
+  // on that stage runs out. wait_limit_ns bounds every pipeline wait of the launch.
+  int stall_kb;
+  unsigned long long wait_limit_ns;
   __device__ __forceinline__ void get(int t, int& m_blk, int& n_blk) const {
     const int per_band = group * num_n;
     const int band = t / per_band;
@@ -120,9 +125,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int m0 = m_blk * kBM;
         const int n0 = n_blk * kBN;
         for (int kb = 0; kb < num_k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status, kStatusTimeoutProducer,
+                                 sched.wait_limit_ns)) {
             ok = false;
             break;
+          }
+          if (kb == sched.stall_kb && t == static_cast<int>(blockIdx.x)) {
+            ++issued;  // left unfilled on purpose (failure-detection testing); nothing is in flight
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
           }
           mbar_arrive_expect_tx(&full[stage], kStageBytes);
           const int k0 = kb * kBK;
@@ -169,14 +183,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int t = blockIdx.x; t < sched.num_tiles && ok; t += gridDim.x, ++local) {
         const int buf = local & 1;
         const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
-        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, status, kStatusTimeoutMma)) {
+        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, status, kStatusTimeoutMma,
+                               sched.wait_limit_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * kBN);
         for (int kb = 0; kb < num_k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusTimeoutMma)) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusTimeoutMma,
+                                 sched.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -211,7 +227,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t acc_phase = static_cast<uint32_t>((local >> 1) & 1);
       int ok = 1;
       if (lane == 0)
-        ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, status, kStatusTimeoutEpilogue) ? 1 : 0;
+        ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, status, kStatusTimeoutEpilogue,
+                                   sched.wait_limit_ns) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
@@ -342,9 +359,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         const int m0 = pm * 2 * kBM + static_cast<int>(rank) * kBM;
         const int n0 = pn * Cfg::kTileN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < num_k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status, kStatusTimeoutProducer)) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, status, kStatusTimeoutProducer,
+                                 sched.wait_limit_ns)) {
             ok = false;
             break;
+          }
+          if (leader && kb == sched.stall_kb && t == pair_id) {
+            ++issued;  // left unfilled on purpose (failure-detection testing); nothing is in flight
+            if (++stage == Cfg::kStages) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
           }
           const uint32_t bar = map_to_cta(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
@@ -407,14 +433,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       for (int t = pair_id; t < sched.num_tiles && ok; t += num_pairs, ++local) {
         const int buf = local % Cfg::kNumAcc;
         const uint32_t acc_phase = static_cast<uint32_t>((local / Cfg::kNumAcc) & 1);
-        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, status, kStatusTimeoutMma)) {
+        if (!mbar_wait_bounded(&acc_empty[buf], acc_phase ^ 1u, abort_flag, status, kStatusTimeoutMma,
+                               sched.wait_limit_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * 256);
         for (int kb = 0; kb < num_k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusTimeoutMma)) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, status, kStatusTimeoutMma,
+                                 sched.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -457,7 +485,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       const uint32_t acc_phase = static_cast<uint32_t>((local / Cfg::kNumAcc) & 1);
       int ok = 1;
       if (lane == 0)
-        ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, status, kStatusTimeoutEpilogue) ? 1 : 0;
+        ok = mbar_wait_bounded(&acc_full[buf], acc_phase, abort_flag, status, kStatusTimeoutEpilogue,
+                                   sched.wait_limit_ns) ? 1 : 0;
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();

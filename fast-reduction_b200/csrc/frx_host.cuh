@@ -122,7 +122,8 @@ int max_pair_clusters(Kernel kernel, std::atomic<int>* cache, int smem_bytes, in
 // 256 x 256 double-buffered tiles (forward); it only applies to the pair kernel.
 template <bool kAMN, bool kBMN, bool kWide, class Epi>
 int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_t K, int group_m,
-                const typename Epi::Params& ep, int* status, cudaStream_t stream) {
+                const typename Epi::Params& ep, int* status, cudaStream_t stream, int stall_kb = -1,
+                uint64_t wait_limit_ns = kWaitLimitNs) {
   FRX_REQUIRE(is_gemm_dtype(a.dtype) && a.dtype == b.dtype, FRX_ERR_INVALID_ARG,
               "GEMM operands must both be bf16 or both fp16 (dtype codes %d, %d)", a.dtype, b.dtype);
   const bool pair = use_pair_kernel();
@@ -140,6 +141,8 @@ int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_
   sched.num_n = static_cast<int>((N + tile_n - 1) / tile_n);
   sched.n256 = static_cast<int>((N + 255) / 256);
   sched.f16 = a.dtype == FRX_DTYPE_F16 ? 1 : 0;
+  sched.stall_kb = stall_kb;
+  sched.wait_limit_ns = wait_limit_ns;
   const int group = pair ? (group_m + 1) / 2 : group_m;
   sched.group = group < 1 ? 1 : (group > sched.num_m ? sched.num_m : group);
   const long long tiles = static_cast<long long>(sched.num_m) * sched.num_n;

@@ -1,7 +1,8 @@
 // Thin inline-PTX wrappers for the sm_100a features the engine uses: mbarriers, TMA tile
 // loads, and the tcgen05 tensor-core / tensor-memory (TMEM) instructions.
 //
-// Every wait in this file is bounded: a wait that does not complete within kWaitLimitNs
+// Every wait in this file is bounded: a wait that does not complete within kWaitLimitNs (or the
+// shorter limit a caller passes)
 // raises a CTA-wide abort flag and ORs an error bit into a caller-provided status word,
 // so a pipeline bug ends the kernel with an error the host can read instead of hanging
 // a shared GPU.
@@ -94,13 +95,13 @@ constexpr uint32_t kSuspendHintNs = 200000;
 // the status bit) when the deadline passes, or returns false at once when another role has
 // already raised the abort flag.
 static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                int* status, int code) {
+                                                int* status, int code, uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       if (status) atomicOr(status, code);
       return false;

@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "frx_column_sums": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _P]),
     "frx_gemm_dhidden_multicast": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I64, _I64, _I64, _P, _P]),
     "frx_split_f32": (_I32, [_P, _I64, _I64, _I64, ctypes.c_uint32, _I32, _P, _I64, _I64, _P]),
+    "frx_test_stalled_fwd": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I64, _P, _P]),
 }
 
 _lib = None

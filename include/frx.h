@@ -220,6 +220,20 @@ FRX_API int frx_fwd_ce_entropy_noalloc(const void* hidden, int64_t ld_hidden, co
                                        float* ce, float* entropy, float* lse, float* log_probs, int* status,
                                        void* stream);
 
+/*
+ * Test hook for failure detection (not part of the computation): runs the bf16 forward of
+ * frx_fwd_partials with k-block `stall_kb` of each CTA pair's first tile left unfilled on purpose, so
+ * the MMA warp's bounded wait on that pipeline stage runs out after `wait_limit_us` microseconds
+ * (every wait of this launch uses that limit). The kernel then takes its abort path: every role
+ * leaves its loop, in-flight copies and MMAs are waited for (bounded), tensor memory is freed, and
+ * FRX_STATUS_TIMEOUT_* bits are set in `status`. Nothing faults and the context stays usable; the
+ * partials of the affected tiles are left unwritten. No counterpart in the reference.
+ */
+FRX_API int frx_test_stalled_fwd(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
+                                 const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
+                                 float* partials, int64_t tile_stride, int stall_kb, int64_t wait_limit_us,
+                                 int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -91,6 +91,10 @@ def test_invalid_arguments_return_codes_without_gpu():
     rc = lib.frx_split_f32(1 << 20, 8, 4, 8, 3, 1, 1 << 21, 8, 32, None)
     assert rc == nat.FRX_ERR_INVALID_ARG  # part selector 3 does not exist
     assert lib.frx_split_f32(None, 8, 0, 8, 0, 1, None, 8, 0, None) == nat.FRX_OK  # empty
+    rc = lib.frx_test_stalled_fwd(1 << 20, 64, 1 << 21, 64, None, 8, 256, 64, 1 << 22, 8, 5, 1000, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # stall past the last k-block
+    rc = lib.frx_test_stalled_fwd(1 << 20, 64, 1 << 21, 64, None, 8, 256, 64, 1 << 22, 8, 0, 0, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG  # wait limit must be positive
 
 
 def test_empty_problems_are_noops():
