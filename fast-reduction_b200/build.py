@@ -1,10 +1,13 @@
 """Builds libfrx.so (the sm_100a CUDA engine behind the C ABI in include/frx.h) in-tree.
 
-Usage:  python fast-reduction_b200/build.py [--verbose] [--force]
+Usage:  python fast-reduction_b200/build.py [--verbose] [--force] [--checked]
 
 The library lands in fast-reduction_b200/fast_reduction/_native/libfrx.so, next to the
 Python package that loads it with ctypes. Objects are rebuilt only when a source or header
-is newer than the library (or with --force).
+is newer than the library (or with --force). --checked builds libfrx_checked.so with
+FRX_CHECKED=1: every entry point verifies that each buffer it will touch lies inside a device
+allocation, and device-side invariant checks report FRX_STATUS_CHECK_FAILED instead of touching
+memory (FRX_LIB=checked makes the Python package load it).
 """
 
 from __future__ import annotations
@@ -22,6 +25,7 @@ CSRC = PKG_ROOT / "csrc"
 INCLUDE = REPO_ROOT / "include"
 OUT_DIR = PKG_ROOT / "fast_reduction" / "_native"
 LIB = OUT_DIR / "libfrx.so"
+LIB_CHECKED = OUT_DIR / "libfrx_checked.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = [
@@ -47,21 +51,24 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
-def _stale() -> bool:
-    if not LIB.exists():
+def _stale(lib: Path) -> bool:
+    if not lib.exists():
         return True
-    lib_mtime = LIB.stat().st_mtime
+    lib_mtime = lib.stat().st_mtime
     deps = list(sources()) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h")) + [Path(__file__)]
     return any(p.stat().st_mtime > lib_mtime for p in deps)
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    if not force and not _stale():
-        return LIB
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False, checked: bool = False) -> Path:
+    lib = LIB_CHECKED if checked else LIB
+    if not force and not _stale(lib):
+        return lib
     OUT_DIR.mkdir(parents=True, exist_ok=True)
     nvcc = _nvcc()
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = lib.with_suffix(".so.tmp")
     cmd = [nvcc, *ARCH_FLAGS, *COMMON_FLAGS, f"-I{INCLUDE}", f"-I{CSRC}", "-shared", "-o", str(tmp)]
+    if checked:
+        cmd.append("-DFRX_CHECKED=1")
     if ptxas_verbose:
         cmd += ["-Xptxas", "-v"]
     cmd += [str(s) for s in sources()]
@@ -73,8 +80,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         raise RuntimeError(f"nvcc failed with exit code {res.returncode}")
     if verbose or ptxas_verbose:
         sys.stderr.write(res.stdout + res.stderr)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 def main() -> None:
@@ -82,8 +89,9 @@ def main() -> None:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-verbose", action="store_true", help="print registers/spills/smem per kernel")
+    ap.add_argument("--checked", action="store_true", help="build libfrx_checked.so (FRX_CHECKED=1)")
     args = ap.parse_args()
-    print(build(force=args.force, verbose=args.verbose, ptxas_verbose=args.ptxas_verbose))
+    print(build(force=args.force, verbose=args.verbose, ptxas_verbose=args.ptxas_verbose, checked=args.checked))
 
 
 if __name__ == "__main__":

@@ -28,7 +28,70 @@ EncodeTiledFn get_encode_fn() {
 }
 
 std::atomic<int> g_sm_count[64];
+
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn get_address_range_fn() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(p);
+  });
+  return fn;
+}
 }  // namespace
+
+namespace {
+// Device ranges that are not driver allocations (module __device__ arrays) but are valid buffers.
+std::mutex g_static_mu;
+struct StaticRange {
+  uintptr_t base;
+  size_t size;
+};
+StaticRange g_static_ranges[64];
+int g_num_static = 0;
+}  // namespace
+
+void register_static_range(const void* base, size_t size) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  for (int i = 0; i < g_num_static; ++i)
+    if (g_static_ranges[i].base == reinterpret_cast<uintptr_t>(base)) return;
+  if (g_num_static < 64) g_static_ranges[g_num_static++] = {reinterpret_cast<uintptr_t>(base), size};
+}
+
+int check_range(const void* p, int64_t bytes, const char* what) {
+  if (p == nullptr || bytes <= 0) return FRX_OK;
+  {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    for (int i = 0; i < g_num_static; ++i) {
+      const StaticRange& r = g_static_ranges[i];
+      if (a >= r.base && a < r.base + r.size)
+        return a + static_cast<uint64_t>(bytes) <= r.base + r.size
+                   ? FRX_OK
+                   : (set_error("%s: %lld bytes from %p run past a %zu-byte static device array", what,
+                                (long long)bytes, p, r.size),
+                      FRX_ERR_INVALID_ARG);
+    }
+  }
+  AddressRangeFn fn = get_address_range_fn();
+  FRX_REQUIRE(fn != nullptr, FRX_ERR_CUDA, "cuMemGetAddressRange is unavailable from the CUDA driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = fn(&base, &size, reinterpret_cast<CUdeviceptr>(p));
+  FRX_REQUIRE(r == CUDA_SUCCESS, FRX_ERR_INVALID_ARG, "%s: %p is not in a device allocation (CUresult %d)", what, p,
+              static_cast<int>(r));
+  const uint64_t end = static_cast<uint64_t>(base) + size;
+  const uint64_t need = reinterpret_cast<uint64_t>(p) + static_cast<uint64_t>(bytes);
+  FRX_REQUIRE(need <= end, FRX_ERR_INVALID_ARG,
+              "%s: %lld bytes from %p run %llu bytes past the end of its device allocation", what,
+              (long long)bytes, p, (unsigned long long)(need - end));
+  return FRX_OK;
+}
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -97,3 +160,5 @@ int encode_f32_2d(CUtensorMap* map, const void* base, int64_t rows, int64_t cols
 extern "C" int frx_abi_version(void) { return FRX_ABI_VERSION; }
 
 extern "C" const char* frx_last_error(void) { return frx::g_last_error; }
+
+extern "C" int frx_check_range(const void* ptr, int64_t bytes) { return frx::check_range(ptr, bytes, "frx_check_range"); }

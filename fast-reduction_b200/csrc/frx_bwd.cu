@@ -184,6 +184,10 @@ static int check_out(void* out, int64_t ld, int64_t cols, int out_dtype, const c
   return FRX_OK;
 }
 
+static int64_t out_elem_bytes(int out_dtype) {
+  return (out_dtype & ~FRX_OUT_ACCUMULATE) == FRX_DTYPE_F32 ? 4 : 2;
+}
+
 static StoreEpilogue::Params store_params(void* out, int64_t ld, int64_t rows, int64_t cols, int out_dtype) {
   StoreEpilogue::Params ep;
   ep.out = out;
@@ -213,6 +217,10 @@ extern "C" int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const v
   FRX_REQUIRE(dlogits != nullptr && weight != nullptr, FRX_ERR_INVALID_ARG, "frx_gemm_dhidden: null input pointer");
   int rc = check_out(d_hidden, ld_d_hidden, hidden_dim, out_dtype, "frx_gemm_dhidden");
   if (rc) return rc;
+  FRX_CHECK_RANGE(dlogits, matrix_bytes(rows, vocab_shard, ld_dlogits, 2), "frx_gemm_dhidden: dlogits");
+  FRX_CHECK_RANGE(weight, matrix_bytes(vocab_shard, hidden_dim, ld_weight, 2), "frx_gemm_dhidden: weight");
+  FRX_CHECK_RANGE(d_hidden, matrix_bytes(rows, hidden_dim, ld_d_hidden, out_elem_bytes(out_dtype)),
+                  "frx_gemm_dhidden: d_hidden");
   Operand a{dlogits, ld_dlogits, rows, vocab_shard, false, in_dtype};  // [rows, V] row-major, K = V contiguous
   Operand b{weight, ld_weight, hidden_dim, vocab_shard, true, in_dtype};  // [V, H] row-major, N = H contiguous
   return launch_gemm<false, true, true, StoreEpilogue>(a, b, rows, hidden_dim, vocab_shard, 8,
@@ -232,6 +240,10 @@ extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const v
   FRX_REQUIRE(dlogits != nullptr && hidden != nullptr, FRX_ERR_INVALID_ARG, "frx_gemm_dweight: null input pointer");
   int rc = check_out(d_weight, ld_d_weight, hidden_dim, out_dtype, "frx_gemm_dweight");
   if (rc) return rc;
+  FRX_CHECK_RANGE(dlogits, matrix_bytes(rows, vocab_shard, ld_dlogits, 2), "frx_gemm_dweight: dlogits");
+  FRX_CHECK_RANGE(hidden, matrix_bytes(rows, hidden_dim, ld_hidden, 2), "frx_gemm_dweight: hidden");
+  FRX_CHECK_RANGE(d_weight, matrix_bytes(vocab_shard, hidden_dim, ld_d_weight, out_elem_bytes(out_dtype)),
+                  "frx_gemm_dweight: d_weight");
   Operand a{dlogits, ld_dlogits, vocab_shard, rows, true, in_dtype};  // [rows, V] row-major, M = V contiguous
   Operand b{hidden, ld_hidden, hidden_dim, rows, true, in_dtype};     // [rows, H] row-major, N = H contiguous
   return launch_gemm<true, true, true, StoreEpilogue>(a, b, vocab_shard, hidden_dim, rows, 8,
@@ -258,6 +270,8 @@ extern "C" int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogit
   ep.cols = static_cast<int>(hidden_dim);
   FRX_REQUIRE(aligned16(d_hidden_mc) && ld_d_hidden % 4 == 0, FRX_ERR_INVALID_ARG,
               "frx_gemm_dhidden_multicast: the multicast buffer must be 16-byte aligned with ld a multiple of 4");
+  FRX_CHECK_RANGE(dlogits, matrix_bytes(rows, vocab_shard, ld_dlogits, 2), "frx_gemm_dhidden_multicast: dlogits");
+  FRX_CHECK_RANGE(weight, matrix_bytes(vocab_shard, hidden_dim, ld_weight, 2), "frx_gemm_dhidden_multicast: weight");
   Operand a{dlogits, ld_dlogits, rows, vocab_shard, false, in_dtype};
   Operand b{weight, ld_weight, hidden_dim, vocab_shard, true, in_dtype};
   // 256 x 256 tiles with the double-buffered TMEM accumulator: each tile's NVLink reductions run

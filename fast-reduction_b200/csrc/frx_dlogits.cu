@@ -130,6 +130,13 @@ extern "C" int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t
   const int64_t out_elem = out_f32 ? 4 : 2;
   const int vec_ok = aligned16(logits) && aligned16(dlogits) && (ld_logits % 4 == 0) &&
                      ((ld_dlogits * out_elem) % 16 == 0);
+  FRX_CHECK_RANGE(logits, matrix_bytes(rows, vocab_shard, ld_logits, 4), "frx_dlogits: logits");
+  FRX_CHECK_RANGE(dlogits, matrix_bytes(rows, vocab_shard, ld_dlogits, out_elem), "frx_dlogits: dlogits");
+  FRX_CHECK_RANGE(target, rows * 8, "frx_dlogits: target");
+  FRX_CHECK_RANGE(lse, rows * 4, "frx_dlogits: lse");
+  FRX_CHECK_RANGE(entropy, rows * 4, "frx_dlogits: entropy");
+  FRX_CHECK_RANGE(g_ce, rows * 4, "frx_dlogits: g_ce");
+  FRX_CHECK_RANGE(g_ent, rows * 4, "frx_dlogits: g_ent");
   const int64_t gx = (vocab_shard + kDlColsPerBlock - 1) / kDlColsPerBlock;
   FRX_REQUIRE(gx < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_dlogits: vocab_shard too large");
   const unsigned gy = static_cast<unsigned>(rows < 65535 ? rows : 65535);

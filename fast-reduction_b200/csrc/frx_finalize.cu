@@ -123,6 +123,13 @@ extern "C" int frx_finalize(const float* partials, int64_t n_tiles, int64_t rows
               "frx_finalize: partials must be 16-byte aligned");
   FRX_REQUIRE(merged == nullptr || aligned16(merged), FRX_ERR_INVALID_ARG,
               "frx_finalize: merged must be 16-byte aligned");
+  FRX_CHECK_RANGE(partials, matrix_bytes(n_tiles, rows, tile_stride, 16), "frx_finalize: partials");
+  FRX_CHECK_RANGE(target, rows * 8, "frx_finalize: target");
+  FRX_CHECK_RANGE(ce, rows * 4, "frx_finalize: ce");
+  FRX_CHECK_RANGE(entropy, rows * 4, "frx_finalize: entropy");
+  FRX_CHECK_RANGE(lse, rows * 4, "frx_finalize: lse");
+  FRX_CHECK_RANGE(log_probs, rows * 4, "frx_finalize: log_probs");
+  FRX_CHECK_RANGE(merged, rows * 16, "frx_finalize: merged");
   const int64_t blocks = (rows + kFinRows - 1) / kFinRows;
   FRX_REQUIRE(blocks < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_finalize: too many rows");
   finalize_kernel<<<static_cast<unsigned>(blocks), kFinRows * kFinSplits, 0, static_cast<cudaStream_t>(stream)>>>(

@@ -80,6 +80,8 @@ struct CEPartialsEpilogue {
     int has_logits;
     int bias_vec;  // bias base 16-byte aligned
     int f16;       // bias is fp16 (else bf16)
+    int n_tiles;   // vocabulary tiles the partials buffer holds (checked builds verify the index)
+    int* status;
   };
 
   template <class Release>
@@ -171,7 +173,8 @@ struct CEPartialsEpilogue {
       }
     }
     release();  // accumulator buffer may now be overwritten by the next tile's MMAs
-    if (row_ok) p.partials[static_cast<int64_t>(n_blk) * p.tile_stride + row] = make_float4(mx, s0 + s1, u0 + u1, zt);
+    if (row_ok && device_check(n_blk < p.n_tiles, p.status))
+      p.partials[static_cast<int64_t>(n_blk) * p.tile_stride + row] = make_float4(mx, s0 + s1, u0 + u1, zt);
   }
 
   // Called once per epilogue warp after its last tile: outstanding logits stores must finish
@@ -211,8 +214,18 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
   FRX_REQUIRE(logits == nullptr || (ld_logits % 4 == 0 && aligned16(logits)), FRX_ERR_INVALID_ARG,
               "frx_fwd_partials: logits must be 16-byte aligned with ld_logits a multiple of 4 (got %lld)",
               (long long)ld_logits);
+  const int64_t n_tiles = (vocab_shard + kBN - 1) / kBN;
+  const int64_t esz = 2;
+  FRX_CHECK_RANGE(hidden, matrix_bytes(rows, hidden_dim, ld_hidden, esz), "frx_fwd_partials: hidden");
+  FRX_CHECK_RANGE(weight, matrix_bytes(vocab_shard, hidden_dim, ld_weight, esz), "frx_fwd_partials: weight");
+  FRX_CHECK_RANGE(bias, vocab_shard * esz, "frx_fwd_partials: bias");
+  FRX_CHECK_RANGE(target, rows * 8, "frx_fwd_partials: target");
+  FRX_CHECK_RANGE(partials, matrix_bytes(n_tiles, rows, tile_stride, 16), "frx_fwd_partials: partials");
+  FRX_CHECK_RANGE(logits, matrix_bytes(rows, vocab_shard, ld_logits, 4), "frx_fwd_partials: logits");
   CEPartialsEpilogue::Params ep;
   memset(&ep, 0, sizeof(ep));
+  ep.n_tiles = static_cast<int>(n_tiles);
+  ep.status = status;
   if (logits != nullptr) {
     const int rc = encode_f32_2d(&ep.tm_logits, logits, rows, vocab_shard, ld_logits, 32, 32);
     if (rc) return rc;

@@ -82,6 +82,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // uniform over the grid, so an early return skips every barrier together
+  if (!device_check(reinterpret_cast<const uint8_t*>(tmem_slot + 2) - smem_raw <=
+                        static_cast<ptrdiff_t>(dynamic_smem_bytes()),
+                    threadIdx.x == 0 ? status : nullptr))
+    return;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -312,6 +317,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* mma_done = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // uniform over the grid (both CTAs of every pair), so an early return skips every barrier together
+  if (!device_check(reinterpret_cast<const uint8_t*>(tmem_slot + 2) - smem_raw <=
+                        static_cast<ptrdiff_t>(dynamic_smem_bytes()),
+                    threadIdx.x == 0 ? status : nullptr))
+    return;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;

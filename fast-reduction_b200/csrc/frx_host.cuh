@@ -41,6 +41,33 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Number of SMs of the current device (cached per device ordinal).
 int sm_count(int* out);
 
+// FRX_OK when [p, p + bytes) lies inside one device allocation (cuMemGetAddressRange), else
+// FRX_ERR_INVALID_ARG with a message naming `what`. NULL / empty ranges pass.
+int check_range(const void* p, int64_t bytes, const char* what);
+
+// Declares a device range that is a valid buffer without being a driver allocation (a module
+// __device__ array) to check_range.
+void register_static_range(const void* base, size_t size);
+
+// Bytes spanned by a row-major matrix of `rows` rows of `cols` elements with row stride `ld`.
+inline int64_t matrix_bytes(int64_t rows, int64_t cols, int64_t ld, int64_t elem) {
+  return rows <= 0 || cols <= 0 ? 0 : ((rows - 1) * ld + cols) * elem;
+}
+
+// Checked builds (FRX_CHECKED=1) verify before every launch that each buffer an entry point will
+// touch lies inside a device allocation; release builds skip the (driver) query.
+#if FRX_CHECKED
+#define FRX_CHECK_RANGE(p, bytes, what)                    \
+  do {                                                     \
+    const int _rc = ::frx::check_range((p), (bytes), (what)); \
+    if (_rc) return _rc;                                   \
+  } while (0)
+#else
+#define FRX_CHECK_RANGE(p, bytes, what) \
+  do {                                  \
+  } while (0)
+#endif
+
 // Encodes a 2-D TMA descriptor over a row-major bf16 (or fp16, `f16`) matrix [rows, cols] with row
 // stride `ld` elements, box [box_rows, box_cols] (box_cols * 2 bytes == 128 for the swizzle),
 // 128-byte swizzle, zero fill outside the matrix.

@@ -45,6 +45,7 @@ static int fwd_scratch_device_ptr(void** out) {
   if (g_scratch_ptr[dev] == nullptr) {
     void* p = nullptr;
     FRX_CUDA_CHECK(cudaGetSymbolAddress(&p, g_fwd_scratch));
+    register_static_range(p, kFwdScratchBytes);
     g_scratch_ptr[dev] = p;
   }
   *out = g_scratch_ptr[dev];

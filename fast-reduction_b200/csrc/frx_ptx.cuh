@@ -23,10 +23,33 @@ enum StatusBits : int {
   kStatusTimeoutEpilogue = 1 << 2,
   kStatusBadTarget = 1 << 3,
   kStatusDrainTimeout = 1 << 4,
+  kStatusCheckFailed = 1 << 5,
 };
 
 // One second: several thousand times longer than the slowest legitimate wait (one
 // 128x256 tile over K = 152064, ~1 ms).
+#ifndef FRX_CHECKED
+#define FRX_CHECKED 0
+#endif
+
+// Device-side invariant checks of checked builds: a failed check ORs FRX_STATUS_CHECK_FAILED into
+// the status word (the caller skips the guarded access); release builds compile them away.
+__device__ __forceinline__ bool device_check(bool ok, int* status) {
+#if FRX_CHECKED
+  if (!ok && status != nullptr) atomicOr(status, static_cast<int>(kStatusCheckFailed));
+  return ok;
+#else
+  (void)status;
+  return true;
+#endif
+}
+
+__device__ __forceinline__ uint32_t dynamic_smem_bytes() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+  return r;
+}
+
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
 constexpr uint64_t kDrainLimitNs = 100ull * 1000ull * 1000ull;
 

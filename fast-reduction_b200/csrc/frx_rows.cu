@@ -184,6 +184,10 @@ extern "C" int frx_logits_partials(const void* logits, int dtype, int64_t ld, in
               "frx_logits_partials: null logits/partials or unaligned partials");
   const int64_t n_tiles = (cols + tile_cols - 1) / tile_cols;
   FRX_REQUIRE(n_tiles < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_logits_partials: too many tiles");
+  const int64_t esz = dtype == FRX_DTYPE_F32 ? 4 : 2;
+  FRX_CHECK_RANGE(logits, matrix_bytes(rows, cols, ld, esz), "frx_logits_partials: logits");
+  FRX_CHECK_RANGE(target, rows * 8, "frx_logits_partials: target");
+  FRX_CHECK_RANGE(partials, matrix_bytes(n_tiles, rows, tile_stride, 16), "frx_logits_partials: partials");
   const int64_t row_blocks = (rows + kRowThreads / 32 - 1) / (kRowThreads / 32);
   const dim3 grid(static_cast<unsigned>(n_tiles), static_cast<unsigned>(row_blocks < 65535 ? row_blocks : 65535));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -294,6 +298,8 @@ extern "C" int frx_column_sums(const void* x, int dtype, int64_t ld, int64_t row
   if (cols == 0) return FRX_OK;
   FRX_REQUIRE(out != nullptr && (x != nullptr || rows == 0), FRX_ERR_INVALID_ARG, "frx_column_sums: null pointer");
   const int vec_ok = aligned16(x) && ld % 8 == 0;
+  FRX_CHECK_RANGE(x, matrix_bytes(rows, cols, ld, 2), "frx_column_sums: x");
+  FRX_CHECK_RANGE(out, cols * 4, "frx_column_sums: out");
   const int64_t blocks = (cols + 255) / 256;
   FRX_REQUIRE(blocks < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_column_sums: too many columns");
   auto kernel = dtype == FRX_DTYPE_F16 ? column_sums_kernel<true> : column_sums_kernel<false>;

@@ -77,6 +77,8 @@ extern "C" int frx_split_f32(const float* x, int64_t ld_x, int64_t rows, int64_t
                 "frx_split_f32: part %d selector must be FRX_PART_HI, _MID or _LO", p);
   const int vec_ok = aligned16(x) && ld_x % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 7u) == 0 &&
                      ld_out % 4 == 0 && part_stride % 4 == 0;
+  FRX_CHECK_RANGE(x, matrix_bytes(rows, cols, ld_x, 4), "frx_split_f32: x");
+  FRX_CHECK_RANGE(out, ((n_parts - 1) * part_stride + matrix_bytes(rows, cols, ld_out, 1)) * 2, "frx_split_f32: out");
   const int64_t gx = (cols + 4 * kSplitThreads - 1) / (4 * kSplitThreads);
   FRX_REQUIRE(gx < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_split_f32: too many columns");
   const unsigned gy = static_cast<unsigned>(rows < 65535 ? rows : 65535);

@@ -14,7 +14,11 @@ from pathlib import Path
 
 import torch
 
-_LIB_PATH = Path(os.environ.get("FRX_LIB", Path(__file__).resolve().parent / "_native" / "libfrx.so"))
+# FRX_LIB: a path to the library, or "checked" for the checked build (libfrx_checked.so: buffer
+# range checks before every launch, device-side invariant checks).
+_NATIVE_DIR = Path(__file__).resolve().parent / "_native"
+_LIB_PATH = Path({"": _NATIVE_DIR / "libfrx.so", "checked": _NATIVE_DIR / "libfrx_checked.so"}.get(
+    os.environ.get("FRX_LIB", ""), os.environ.get("FRX_LIB", "")))
 
 FRX_OK = 0
 FRX_ERR_INVALID_ARG = 1
@@ -39,6 +43,7 @@ FRX_STATUS_TIMEOUT_MMA = 2
 FRX_STATUS_TIMEOUT_EPILOGUE = 4
 FRX_STATUS_BAD_TARGET = 8
 FRX_STATUS_DRAIN_TIMEOUT = 16
+FRX_STATUS_CHECK_FAILED = 32
 
 _STATUS_NAMES = {
     FRX_STATUS_TIMEOUT_PRODUCER: "TMA producer wait timed out",
@@ -46,6 +51,7 @@ _STATUS_NAMES = {
     FRX_STATUS_TIMEOUT_EPILOGUE: "epilogue wait timed out",
     FRX_STATUS_BAD_TARGET: "target id outside [0, vocab_size) and not ignore_index",
     FRX_STATUS_DRAIN_TIMEOUT: "in-flight copies did not drain after an abort",
+    FRX_STATUS_CHECK_FAILED: "a device-side invariant check of the checked build failed",
 }
 
 # Every exported symbol with its ctypes signature: (restype, argtypes).
@@ -71,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     "frx_gemm_dhidden_multicast": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I64, _I64, _I64, _P, _P]),
     "frx_split_f32": (_I32, [_P, _I64, _I64, _I64, ctypes.c_uint32, _I32, _P, _I64, _I64, _P]),
     "frx_test_stalled_fwd": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I64, _P, _P]),
+    "frx_check_range": (_I32, [_P, _I64]),
 }
 
 _lib = None

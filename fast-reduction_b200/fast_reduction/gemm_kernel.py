@@ -191,8 +191,9 @@ def forward_stats(
     for start in range(0, B, chunk):
         end = min(start + chunk, B)
         rows = end - start
-        ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
-                         bias=bias)
+        with ops.phase("frx.forward.chunk"):
+            ops.fwd_partials(hidden_2d[start:end], weight, target_1d[start:end], partials, chunk, vocab_offset,
+                             bias=bias)
         ops.finalize(
             partials, T, rows, chunk,
             target=target_1d[start:end], vocab_size=vocab_size, ignore_index=ignore_index,
@@ -533,11 +534,13 @@ def fwd_bwd_shard(
         logits, partials = logits_bufs[buf], partials_bufs[buf]
         if done[buf] is not None:
             main.wait_event(done[buf])
-        ops.fwd_partials(x_fwd[start:end], w_fwd, target_1d[start:end], partials, chunk, vocab_offset,
-                         logits=logits, bias=fwd_bias)
+        with ops.phase("frx.train.forward_chunk"):
+            ops.fwd_partials(x_fwd[start:end], w_fwd, target_1d[start:end], partials, chunk, vocab_offset,
+                             logits=logits, bias=fwd_bias)
 
         def run_dlogits(logits=logits, partials=partials, start=start, end=end, rows=rows):
-            stats_fn(start, end, partials, T, chunk)
+            with ops.phase("frx.train.stats"):
+                stats_fn(start, end, partials, T, chunk)
             ops.dlogits(
                 logits, target_1d[start:end], lse[start:end], entropy[start:end],
                 dz32 if f32 else dz[start:end],
@@ -573,21 +576,23 @@ def fwd_bwd_shard(
         dh_pairs = [(dz_parts[i], w_parts[j]) for i, j in zip(ops.SPLIT_LEFT, ops.SPLIT_RIGHT)]
     else:
         dh_pairs = [(dz, weight)]
-    if dhidden_fn is not None:
-        d_hidden, pending = dhidden_fn(dh_pairs)
-    else:
-        d_hidden = torch.empty(B, H, device=dev, dtype=hidden_2d.dtype)
-        for i, (a_op, b_op) in enumerate(dh_pairs):
-            ops.gemm_dhidden(a_op, b_op, d_hidden, rows=B, vocab_shard=V, accumulate=i > 0)
-        pending = None
+    with ops.phase("frx.train.dhidden"):
+        if dhidden_fn is not None:
+            d_hidden, pending = dhidden_fn(dh_pairs)
+        else:
+            d_hidden = torch.empty(B, H, device=dev, dtype=hidden_2d.dtype)
+            for i, (a_op, b_op) in enumerate(dh_pairs):
+                ops.gemm_dhidden(a_op, b_op, d_hidden, rows=B, vocab_shard=V, accumulate=i > 0)
+            pending = None
     d_weight = torch.empty(V, H, device=dev, dtype=weight.dtype)
-    if f32:
-        del w_parts, dh_pairs
-        x_parts = _fp32_parts(hidden_2d)
-        for n_, (i, j) in enumerate(zip(ops.SPLIT_LEFT, ops.SPLIT_RIGHT)):
-            ops.gemm_dweight(dz_parts[i], x_parts[j], d_weight, rows=B, vocab_shard=V, accumulate=n_ > 0)
-    else:
-        ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
+    with ops.phase("frx.train.dweight"):
+        if f32:
+            del w_parts, dh_pairs
+            x_parts = _fp32_parts(hidden_2d)
+            for n_, (i, j) in enumerate(zip(ops.SPLIT_LEFT, ops.SPLIT_RIGHT)):
+                ops.gemm_dweight(dz_parts[i], x_parts[j], d_weight, rows=B, vocab_shard=V, accumulate=n_ > 0)
+        else:
+            ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
     d_bias = None
     if bias is not None:
         d_bias32 = torch.empty(V, device=dev, dtype=torch.float32)

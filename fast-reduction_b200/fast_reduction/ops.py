@@ -8,6 +8,9 @@ fast_reduction/gemm_ce_entropy_finalize.py:123-148, cute_dlogits.py:121-159).
 
 from __future__ import annotations
 
+import contextlib
+import os
+
 import torch
 
 from . import _native as nat
@@ -28,14 +31,45 @@ def set_launch_observer(observer):
     return prev
 
 
+# NVTX ranges (visible in Nsight Systems / Nsight Compute timelines): one per libfrx launch, named
+# "frx.<entry point>", inside the phase ranges of the Python layer. FRX_NVTX=0 turns them off.
+_NVTX = os.environ.get("FRX_NVTX", "1") != "0"
+
+
+def _nvtx_push(name: str) -> bool:
+    if not _NVTX:
+        return False
+    try:
+        torch.cuda.nvtx.range_push(name)
+        return True
+    except Exception:  # a torch build without NVTX
+        return False
+
+
+@contextlib.contextmanager
+def phase(name: str):
+    """NVTX range around one phase of the path (e.g. "frx.train.dhidden")."""
+    pushed = _nvtx_push(name)
+    try:
+        yield
+    finally:
+        if pushed:
+            torch.cuda.nvtx.range_pop()
+
+
 def _launch(name: str, dev: torch.device, call) -> int:
-    obs = _observer
-    if obs is None:
-        return call()
-    obs.before(name, dev)
-    rc = call()
-    obs.after(name, dev)
-    return rc
+    pushed = _nvtx_push("frx." + name)
+    try:
+        obs = _observer
+        if obs is None:
+            return call()
+        obs.before(name, dev)
+        rc = call()
+        obs.after(name, dev)
+        return rc
+    finally:
+        if pushed:
+            torch.cuda.nvtx.range_pop()
 
 
 def n_vocab_tiles(vocab_shard: int) -> int:

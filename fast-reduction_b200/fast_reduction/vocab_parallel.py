@@ -149,7 +149,8 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
     def exchange_stats(start, end, partials, T, chunk):
         rows = end - start
         ops.finalize(partials, T, rows, chunk, merged=local[start:end])
-        gathered = _gather_stats(local[start:end], group)
+        with ops.phase("frx.vp.stats_allgather"):
+            gathered = _gather_stats(local[start:end], group)
         merge_rows(gathered, target_1d[start:end], vocab_size, ignore_index, ce=ce[start:end],
                    entropy=ent[start:end], lse=lse[start:end])
 
@@ -207,7 +208,7 @@ def _allreduce_async(t: Tensor, group) -> _PendingAllReduce:
         _side_streams[dev] = side
     main = torch.cuda.current_stream()
     side.wait_stream(main)
-    with torch.cuda.stream(side):
+    with torch.cuda.stream(side), ops.phase("frx.vp.dhidden_allreduce"):
         dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
         done = torch.cuda.Event()
         done.record(side)

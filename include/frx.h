@@ -71,6 +71,7 @@ extern "C" {
 #define FRX_STATUS_TIMEOUT_EPILOGUE 4
 #define FRX_STATUS_BAD_TARGET 8
 #define FRX_STATUS_DRAIN_TIMEOUT 16
+#define FRX_STATUS_CHECK_FAILED 32 /* a device-side invariant check of a checked build failed */
 
 /* ABI version of the loaded library (FRX_ABI_VERSION it was built with). */
 FRX_API int frx_abi_version(void);
@@ -219,6 +220,14 @@ FRX_API int frx_fwd_ce_entropy_noalloc(const void* hidden, int64_t ld_hidden, co
                                        int64_t vocab_size, int64_t hidden_dim, int64_t ignore_index,
                                        float* ce, float* entropy, float* lse, float* log_probs, int* status,
                                        void* stream);
+
+/*
+ * FRX_OK when the `bytes` bytes from `ptr` lie inside one device allocation (cuMemGetAddressRange),
+ * else FRX_ERR_INVALID_ARG with the overrun in frx_last_error(). Checked builds (libfrx_checked.so,
+ * built with FRX_CHECKED=1) run this on every buffer before each launch; it is exported by every
+ * build as a debugging aid. No counterpart in the reference.
+ */
+FRX_API int frx_check_range(const void* ptr, int64_t bytes);
 
 /*
  * Test hook for failure detection (not part of the computation): runs the bf16 forward of

@@ -104,3 +104,18 @@ def test_empty_problems_are_noops():
     assert lib.frx_fwd_partials(None, 0, None, 0, 0, None, None, 0, 10, 64, 0, None, 0, None, 0, None,
                                 None) == nat.FRX_OK
     assert lib.frx_finalize(None, 0, 0, 0, 0, None, 0, 0, None, None, None, None, None, None, None) == nat.FRX_OK
+
+
+def test_checked_build_exports_the_same_symbols():
+    """libfrx_checked.so (FRX_CHECKED=1) is a drop-in for libfrx.so: same exported entry points."""
+    import sys
+
+    sys.path.insert(0, str(REPO / "fast-reduction_b200"))
+    import build as frx_build
+
+    path = frx_build.build(checked=True)
+    lib = ctypes.CDLL(str(path))
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} missing from the checked build"
+    lib.frx_check_range.argtypes = [ctypes.c_void_p, ctypes.c_int64]
+    assert lib.frx_check_range(None, 0) == 0
