@@ -193,6 +193,32 @@ def test_megakernel_chunked_equals_unchunked_and_dloss_scaling():
     torch.testing.assert_close(grads[2][1].float(), 3.0 * grads[0][1].float(), atol=1e-6, rtol=1e-2)
 
 
+def test_side_stream_overlap_is_race_free(monkeypatch):
+    """The per-chunk statistics and dlogits run on a side stream under the next chunk's GEMM, with
+    double-buffered logits / partials. Racing buffer reuse would change results: gradients with the
+    overlap, twice, must equal the serialised schedule bit for bit (8 chunks, each kernel long
+    enough for the streams to really overlap)."""
+    from fast_reduction import gemm_kernel as gk
+
+    h, w, t = rm.make_inputs(4096, 1024, 32000, seed=8, weight_std=0.05, ignore_frac=0.02)
+    hd0, wd0, td = h.to(DEV), w.to(DEV), t.to(DEV)
+
+    def grads():
+        hd = hd0.clone().requires_grad_(True)
+        wd = wd0.clone().requires_grad_(True)
+        loss, ce, ent = gk.gemm_megakernel_fast(hd, wd, td, chunk_size=512)
+        loss.backward()
+        torch.cuda.synchronize()
+        return ce, ent, hd.grad, wd.grad
+
+    monkeypatch.setattr(gk, "_OVERLAP_DLOGITS", True)
+    a, b = grads(), grads()
+    monkeypatch.setattr(gk, "_OVERLAP_DLOGITS", False)
+    serial = grads()
+    for x, y, z in zip(a, b, serial):
+        assert torch.equal(x, y) and torch.equal(x, z)
+
+
 def test_differentiable_matches_fp32_with_per_row_upstream_grads():
     """gemm_fused_ce_entropy_differentiable (reference gemm_kernel.py:541-582): backward with
     arbitrary per-row g_ce, g_ent and g_lp (log_probs = -ce, so the CE weight is g_ce - g_lp)."""
