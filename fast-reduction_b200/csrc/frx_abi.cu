@@ -108,6 +108,14 @@ bool use_pair_kernel() {
   return pair;
 }
 
+int env_int(const char* name, int fallback) {
+  const char* v = getenv(name);
+  if (v == nullptr || *v == '\0') return fallback;
+  char* end = nullptr;
+  const long x = strtol(v, &end, 10);
+  return (end != v && x > 0 && x < (1 << 20)) ? static_cast<int>(x) : fallback;
+}
+
 int sm_count(int* out) {
   int dev = 0;
   FRX_CUDA_CHECK(cudaGetDevice(&dev));
@@ -161,4 +169,6 @@ extern "C" int frx_abi_version(void) { return FRX_ABI_VERSION; }
 
 extern "C" const char* frx_last_error(void) { return frx::g_last_error; }
 
-extern "C" int frx_check_range(const void* ptr, int64_t bytes) { return frx::check_range(ptr, bytes, "frx_check_range"); }
+extern "C" int frx_check_range(const void* ptr, int64_t bytes) {
+  return frx::check_range(ptr, bytes, "frx_check_range");
+}

@@ -244,7 +244,9 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
   Operand b{weight, ld_weight, vocab_shard, hidden_dim, false, dtype};
   // A band of up to 64 row blocks (8192 rows, 64 MiB of bf16 hidden at H=4096) stays in L2
   // while the CTAs sweep the vocabulary.
-  return launch_gemm<false, false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, 64, ep, status,
+  // FRX_FWD_GROUP_M (tuning only) overrides the band height in 128-row blocks.
+  static const int group_m = env_int("FRX_FWD_GROUP_M", 64);
+  return launch_gemm<false, false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, group_m, ep, status,
                                                               static_cast<cudaStream_t>(stream), stall_kb,
                                                               wait_limit_ns);
 }

@@ -114,6 +114,9 @@ inline int encode_operand(CUtensorMap* map, const Operand& op, int tile_mn) {
 // FRX_GEMM_VARIANT environment variable ("pair" / "single") overrides it, for tuning only.
 bool use_pair_kernel();
 
+// Positive integer from the environment variable `name`, else `fallback` (tuning knobs only).
+int env_int(const char* name, int fallback);
+
 // Co-resident 2-CTA clusters of `kernel` on the current device (cached per device).
 template <class Kernel>
 int max_pair_clusters(Kernel kernel, std::atomic<int>* cache, int smem_bytes, int* out) {
