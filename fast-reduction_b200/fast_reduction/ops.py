@@ -182,14 +182,16 @@ def finalize(
     for name, t in (("ce", ce), ("entropy", entropy), ("lse", lse), ("log_probs", log_probs)):
         if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < rows):
             raise ValueError(f"{name} must be contiguous float32 with >= rows elements")
-    if merged is not None and (merged.dtype != torch.float32 or not merged.is_contiguous() or merged.numel() < 4 * rows):
+    if merged is not None and (merged.dtype != torch.float32 or not merged.is_contiguous()
+                               or merged.numel() < 4 * rows):
         raise ValueError("merged must be contiguous float32 [rows, 4]")
     if target is not None and (target.dtype != torch.int64 or not target.is_contiguous() or target.numel() < rows):
         raise ValueError("target must be a contiguous int64 tensor with one id per row")
     lib = nat.load()
     rc = _launch("finalize", dev, lambda: lib.frx_finalize(
         partials.data_ptr(), n_tiles, rows, tile_stride,
-        (nat.FRX_PARTIALS_REF_LAYOUT if ref_layout else 0) | (nat.FRX_IGNORE_NEGATIVE_TARGETS if ignore_negative else 0),
+        (nat.FRX_PARTIALS_REF_LAYOUT if ref_layout else 0)
+        | (nat.FRX_IGNORE_NEGATIVE_TARGETS if ignore_negative else 0),
         nat.ptr(target), vocab_size, ignore_index, nat.ptr(ce), nat.ptr(entropy), nat.ptr(lse), nat.ptr(log_probs),
         nat.ptr(merged), nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
@@ -312,7 +314,8 @@ def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, r
     nat.check(rc, "frx_gemm_dweight")
 
 
-_LOGITS_DTYPES = {torch.bfloat16: nat.FRX_DTYPE_BF16, torch.float16: nat.FRX_DTYPE_F16, torch.float32: nat.FRX_DTYPE_F32}
+_LOGITS_DTYPES = {torch.bfloat16: nat.FRX_DTYPE_BF16, torch.float16: nat.FRX_DTYPE_F16,
+                  torch.float32: nat.FRX_DTYPE_F32}
 
 
 def logits_partials(logits: torch.Tensor, target: torch.Tensor | None, partials: torch.Tensor, tile_cols: int,

@@ -97,8 +97,8 @@ FRX_API const char* frx_last_error(void);
  *   logits   optional fp32 [rows, ld_logits] output of every z (NULL: logits never leave the chip)
  */
 FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
-                     int dtype, const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard, int64_t hidden_dim,
-                     int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
+                     int dtype, const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
+                     int64_t hidden_dim, int64_t vocab_offset, float* partials, int64_t tile_stride, float* logits,
                      int64_t ld_logits, int* status, void* stream);
 
 /*

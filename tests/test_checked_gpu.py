@@ -44,8 +44,9 @@ def test_parity_suites_pass_under_the_checked_build():
               "tests/test_zz_no_alloc.py"]
     code = ("import sys; from fast_reduction import _native as nat; "
             "assert nat.library_path().name == 'libfrx_checked.so', nat.library_path()")
-    probe = subprocess.run([sys.executable, "-c", code], cwd=REPO, env=dict(env, PYTHONPATH=str(REPO / "fast-reduction_b200")),
-                           capture_output=True, text=True, timeout=300)
+    probe_env = dict(env, PYTHONPATH=str(REPO / "fast-reduction_b200"))
+    probe = subprocess.run([sys.executable, "-c", code], cwd=REPO, env=probe_env, capture_output=True, text=True,
+                           timeout=300)
     assert probe.returncode == 0, probe.stderr[-2000:]
     out = subprocess.run([sys.executable, "-m", "pytest", *suites, "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider"],
                          cwd=REPO, env=env, capture_output=True, text=True, timeout=1200)
