@@ -142,7 +142,9 @@ struct CEPartialsEpilogue {
       }
     }
     const float mx = fmaxf(mx0, mx1);
-    const float mx_l2 = mx * kLog2e;
+    // exp(z - m) as 2^((z - m) log2 e) with z - m formed first: the largest logit gets exactly 1 and
+    // the error does not grow with |m| (folding m into one FMA, z log2e - m log2e, would carry the
+    // rounding of m log2e, about |m| 2^-24).
     float s0 = 0.f, s1 = 0.f, u0 = 0.f, u1 = 0.f;
 #pragma unroll 1
     for (int c = 0; c < kBN / 32; ++c) {
@@ -154,20 +156,22 @@ struct CEPartialsEpilogue {
       if (lim >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const float e0 = ex2_approx(fmaf(v[j], kLog2e, -mx_l2));
-          const float e1 = ex2_approx(fmaf(v[j + 1], kLog2e, -mx_l2));
+          const float d0 = v[j] - mx, d1 = v[j + 1] - mx;
+          const float e0 = ex2_approx(d0 * kLog2e);
+          const float e1 = ex2_approx(d1 * kLog2e);
           s0 += e0;
           s1 += e1;
-          u0 = fmaf(v[j] - mx, e0, u0);
-          u1 = fmaf(v[j + 1] - mx, e1, u1);
+          u0 = fmaf(d0, e0, u0);
+          u1 = fmaf(d1, e1, u1);
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           if (j < lim) {
-            const float e = ex2_approx(fmaf(v[j], kLog2e, -mx_l2));
+            const float d = v[j] - mx;
+            const float e = ex2_approx(d * kLog2e);
             s0 += e;
-            u0 = fmaf(v[j] - mx, e, u0);
+            u0 = fmaf(d, e, u0);
           }
         }
       }

@@ -54,13 +54,13 @@ __device__ __forceinline__ void online_add(OnlineStat& st, const float (&v)[N], 
     st.m = vm;
   }
   if (vm == -INFINITY) return;
-  const float ml = st.m * kLog2e;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
     if (i < n_valid) {
-      const float e = ex2_approx(fmaf(v[i], kLog2e, -ml));
+      const float d = v[i] - st.m;  // formed first: exact 1 at the max, error independent of |m|
+      const float e = ex2_approx(d * kLog2e);
       st.s += e;
-      st.u = fmaf(v[i] - st.m, e, st.u);
+      st.u = fmaf(d, e, st.u);
     }
   }
 }

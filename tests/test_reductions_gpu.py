@@ -64,3 +64,25 @@ def test_uniform_logits_entropy_is_log_n():
     ent = entropy_fwd(x)
     torch.testing.assert_close(ent.double(), torch.full((8,), math.log(50000), device=DEV, dtype=torch.float64),
                                atol=1e-5, rtol=1e-6)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_rising_and_wide_range_logits(dtype):
+    """Rows whose running max rises at every vector (the online reference point is rescaled again and
+    again), rows spanning +-1e4, and N = 65536 (the reference's large-vocabulary regression sizes)."""
+    from fast_reduction.cute_cross_entropy import ce_entropy_fwd_with_lse
+
+    N = 65536
+    rising = torch.linspace(-60.0, 60.0, N, device=DEV)
+    falling = rising.flip(0)
+    g = torch.Generator(device=DEV).manual_seed(1)
+    wide = torch.randn(N, device=DEV, generator=g) * 1e4
+    spiky = torch.randn(N, device=DEV, generator=g)
+    spiky[::4096] = 80.0
+    x = torch.stack([rising, falling, wide, spiky, rising * 1e-3]).to(dtype)
+    t = torch.tensor([N - 1, 0, 5, 4096, 17], device=DEV)
+    ce, ent, lse = ce_entropy_fwd_with_lse(x, t)
+    ce_r, ent_r, lse_r = _ref(x, t)
+    torch.testing.assert_close(lse.double(), lse_r, atol=1e-3, rtol=2e-6)
+    torch.testing.assert_close(ce.double(), ce_r, atol=1e-3, rtol=2e-5)
+    torch.testing.assert_close(ent.double(), ent_r, atol=2e-4, rtol=2e-5)
