@@ -100,6 +100,8 @@ def vocab_parallel_ce_entropy(
     """Forward over this rank's vocabulary slice; returns the full (ce_loss, entropy, log_probs)
     (identical on every rank), shaped like hidden_states.shape[:-1]. ``bias_shard`` is the bias of
     this rank's vocabulary rows, if any."""
+    if weight_shard.dim() == 2 and weight_shard.shape[0] == 0:
+        raise ValueError("every rank needs a non-empty vocabulary slice (vocab_size >= world size)")
     batch_shape, hidden_2d, weight_shard, target_1d, bias_shard = gk._prepare(hidden_states, weight_shard, target,
                                                                               bias_shard, allow_host=True)
     B = hidden_2d.shape[0]

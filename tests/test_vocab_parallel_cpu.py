@@ -134,3 +134,12 @@ def test_failed_rank_surfaces_as_error_not_hang():
             p.kill()
     assert results[1][0] == "raised"
     assert results[0][0] == "raised", results
+
+
+def test_empty_shard_is_rejected_before_any_collective():
+    from fast_reduction.vocab_parallel import vocab_parallel_ce_entropy
+
+    h = torch.randn(4, 16).to(torch.bfloat16)
+    w = torch.empty(0, 16, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="non-empty vocabulary slice"):
+        vocab_parallel_ce_entropy(h, w, torch.zeros(4, dtype=torch.int64), 0, 3)
