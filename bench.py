@@ -38,7 +38,7 @@ import torch.distributed as dist  # noqa: E402
 
 METRIC = "fwd & fwd+bwd ms @B32768 H4096 V128256 bf16; % dense BF16 tensor peak"
 WORKLOAD = "configs[1] forward headline: B=32768 H=4096 V=128256 bf16 chunk 4096"
-# The reference's own published numbers for this metric and shape (Level-5
+# The reference's own published numbers for this metric and shape (its README.md:15 and :32: Level-5
 # forward and 5M training step at B=32768, H=4096, V=128256, bf16, chunk 4096, on one H100).
 REFERENCE_PUBLISHED_MS = {"fwd": 67.0, "fwd_bwd": 243.0}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
@@ -503,7 +503,7 @@ def run_ours(args, world, rank, local):
         "higher_is_better": False,
         "scaling": "strong",
         "vs_baseline": round(fwd_ms / REFERENCE_PUBLISHED_MS["fwd"], 4) if headline_shape else None,
-        "vs_baseline_source": ("reference's published Level-5 forward, 67 ms on one H100 (BASELINE.md); "
+        "vs_baseline_source": ("reference's published Level-5 forward, 67 ms on one H100 (its README.md:15); "
                                "value / 67, lower is better") if headline_shape else None,
         "dtype": "bf16",
         "data": "synthetic (seeded: hidden N(0,1), weight N(0,0.02), uniform targets)",

@@ -17,7 +17,7 @@ Engine (all device work is libfrx, sm_100a):
             over the full batch (d_weight accumulates over every row in TMEM: no fp32 d_weight
             read-modify-write per chunk, no transposed weight copy).
 
-Semantics chosen where the reference is inconsistent (documented in DESIGN.md):
+Semantics chosen where the reference is inconsistent:
   * ignore_index (default -100): ce = 0, log_probs = 0 and no CE gradient for such rows; the
     entropy and its gradient are kept (torch nll_loss semantics, reference baseline.py:80).
   * bias: the reference accepts it but never adds it to the logits in its GEMM path

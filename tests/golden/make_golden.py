@@ -1,7 +1,7 @@
 """Generates the golden fixtures in tests/golden/ by running the REFERENCE's own code.
 
 Run in the build container, where the reference checkout is readable:
-    python tests/golden/make_golden.py [--ref /path/to/fast-reduction]
+    python tests/golden/make_golden.py --ref /path/to/fast-reduction
 
 It imports the reference's fast_reduction/baseline.py by file path (pure torch, runs on CPU)
 under a private module name and records its outputs on small seeded inputs. The fixtures are
@@ -40,7 +40,7 @@ def digest(*tensors: torch.Tensor) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of a checkout of the reference (justinchiu/fast-reduction)")
     args = ap.parse_args()
     ref = load_reference_baseline(Path(args.ref))
     torch.set_num_threads(8)
