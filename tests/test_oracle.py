@@ -158,7 +158,7 @@ def test_cfg0_inputs_regenerate_and_match_reference_outputs():
     assert torch.equal(ce, torch.from_numpy(GOLDEN["cfg0_ce"]))
     assert torch.equal(ent, torch.from_numpy(GOLDEN["cfg0_ent"]))
     assert torch.equal(lp, torch.from_numpy(GOLDEN["cfg0_lp"]))
-    # fp32 ground truth vs the reference's bf16-logit chunked path (survey: ~1.2e-3 / 5e-5)
+    # fp32 ground truth vs the reference's bf16-logit chunked path (about 1.2e-3 / 5e-5 at this shape)
     ce32, ent32, _, _ = rm.fp32_reference(h, w, t)
     assert (ce - ce32).abs().mean() < 2e-3
     assert (ent - ent32).abs().mean() < 1e-4
