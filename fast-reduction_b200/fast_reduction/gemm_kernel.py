@@ -684,3 +684,4 @@ def gemm_megakernel_fast(
 # megakernel (gradients precomputed in forward, backward scales by dloss); here both names run
 # the same sm_100a training path.
 gemm_fused_ce_entropy_fast = gemm_megakernel_fast
+GemmFusedCEEntropyFast = GemmMegakernel

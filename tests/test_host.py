@@ -94,6 +94,8 @@ def test_tile_helpers():
 def test_lazy_exports():
     import fast_reduction
 
+    assert gk.GemmFusedCEEntropyFast is gk.GemmMegakernel
+
     assert fast_reduction.gemm_fused_ce_entropy is gk.gemm_fused_ce_entropy
     assert fast_reduction.gemm_megakernel_fast is gk.gemm_megakernel_fast
     with pytest.raises(AttributeError):
