@@ -167,6 +167,50 @@ class KernelTimer:
         return out
 
 
+_PROBE_SMS = 256
+# Dense bf16 tensor work per SM per clock: B200's nominal 2.25 PFLOP/s dense bf16 is 148 SMs x 8,192
+# FLOP x 1.855 GHz; the forward GEMM's ncu tensor-pipe utilisation agrees with this rate.
+_FLOP_PER_CLK_SM = 8192
+
+
+def _clock_frac(tflops_per_gpu: float, clocks) -> float | None:
+    """Achieved TFLOP/s per GPU over the dense bf16 peak at the SM clock the timed region actually ran
+    (frx_clock_probe): how close the kernels come to what the power cap lets the clock allow."""
+    mhz = (clocks or {}).get("sm_mhz_effective")
+    if not mhz:
+        return None
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return round(tflops_per_gpu / (sms * _FLOP_PER_CLK_SM * mhz * 1e6 / 1e12), 4)
+
+
+def _clock_probe_start():
+    """Stamps every SM's %clock64 with %globaltimer (frx_clock_probe) before a timed region."""
+    from fast_reduction import _native as nat
+
+    buf = torch.zeros(2, 2 * _PROBE_SMS, dtype=torch.int64, device="cuda")
+    nat.check(nat.load().frx_clock_probe(buf[0].data_ptr(), _PROBE_SMS, nat.stream_of(buf.device)),
+              "frx_clock_probe")
+    return buf
+
+
+def _clock_probe_stop(buf):
+    """Second stamp after the region; returns a function giving the region's average SM clock in MHz
+    (median over the SMs stamped both times; cycle counters are per SM)."""
+    from fast_reduction import _native as nat
+
+    nat.check(nat.load().frx_clock_probe(buf[1].data_ptr(), _PROBE_SMS, nat.stream_of(buf.device)),
+              "frx_clock_probe")
+
+    def read():
+        b = buf.cpu().view(2, _PROBE_SMS, 2)
+        rates = [(int(b[1, s, 0]) - int(b[0, s, 0])) / (int(b[1, s, 1]) - int(b[0, s, 1])) * 1000.0
+                 for s in range(_PROBE_SMS)
+                 if int(b[0, s, 1]) and int(b[1, s, 1]) and int(b[1, s, 1]) > int(b[0, s, 1])]
+        return round(statistics.median(rates), 1) if rates else None
+
+    return read
+
+
 def time_steps(step, steps: int, warmup: int, world: int, timer: KernelTimer | None = None, sampler=None):
     from fast_reduction import ops
 
@@ -180,14 +224,18 @@ def time_steps(step, steps: int, warmup: int, world: int, timer: KernelTimer | N
     prev = ops.set_launch_observer(timer) if timer is not None else None
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    probe = _clock_probe_start()
     start.record()
     for _ in range(steps):
         step()
     end.record()
+    effective_mhz = _clock_probe_stop(probe)
     torch.cuda.synchronize()
     if timer is not None:
         ops.set_launch_observer(prev)
     clocks = sampler.stop() if sampler is not None else None
+    if clocks is not None:
+        clocks["sm_mhz_effective"] = effective_mhz()
     barrier(world)
     ms = start.elapsed_time(end) / steps
     return max_over_ranks(ms, world), clocks
@@ -424,6 +472,7 @@ def run_ours(args, world, rank, local):
         fb = {"ms": round(fb_ms, 3), "tflops": round(flops_fb / (fb_ms / 1000.0) / 1e12, 1),
               "frac_of_peak": round(flops_fb / (fb_ms / 1000.0) / 1e12 / (peak_tf * world), 4),
               "frac_of_sustained_peak": round(flops_fb / (fb_ms / 1000.0) / 1e12 / (peak_sus * world), 4),
+              "frac_of_clock_limited_peak": _clock_frac(flops_fb / (fb_ms / 1000.0) / 1e12 / world, fb_clocks),
               "steps": fb_steps,
               "workload": "configs[2] gemm_megakernel_fast + loss.backward(), ce_weight 1, ent_weight -1",
               "peak_extra_mem_gb": round(peak_extra_fb, 3),
@@ -513,6 +562,7 @@ def run_ours(args, world, rank, local):
         "tflops": round(tflops, 1),
         "frac_of_peak": round(tflops / (peak_tf * world), 4),
         "frac_of_sustained_peak": round(tflops / (peak_sus * world), 4),
+        "frac_of_clock_limited_peak": _clock_frac(tflops / world, clocks),
         "peak_bf16_tflops": peak_tf,
         "peak_bf16_tflops_sustained": peak_sus,
         "peak_source": peaks.get("source"),

@@ -172,3 +172,31 @@ extern "C" const char* frx_last_error(void) { return frx::g_last_error; }
 extern "C" int frx_check_range(const void* ptr, int64_t bytes) {
   return frx::check_range(ptr, bytes, "frx_check_range");
 }
+
+namespace frx {
+
+// One thread per block stamps its SM's cycle counter and the global nanosecond timer into the SM's
+// slot. Cycle counters are per SM, so a clock is only read from two stamps of the same SM.
+__global__ void clock_probe_kernel(unsigned long long* out, int max_sms) {
+  if (threadIdx.x != 0) return;
+  unsigned int smid;
+  unsigned long long c, t;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(c));
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  if (smid < static_cast<unsigned int>(max_sms)) {
+    out[2 * smid] = c;
+    out[2 * smid + 1] = t;
+  }
+}
+
+}  // namespace frx
+
+extern "C" int frx_clock_probe(uint64_t* out, int max_sms, void* stream) {
+  FRX_REQUIRE(out != nullptr && max_sms >= 1 && max_sms <= 4096, FRX_ERR_INVALID_ARG,
+              "frx_clock_probe: need an output of 2 * max_sms stamps, 1 <= max_sms <= 4096");
+  frx::clock_probe_kernel<<<static_cast<unsigned>(4 * max_sms), 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<unsigned long long*>(out), max_sms);
+  FRX_CUDA_CHECK(cudaGetLastError());
+  return FRX_OK;
+}

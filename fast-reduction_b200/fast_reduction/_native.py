@@ -78,6 +78,7 @@ SIGNATURES: dict[str, tuple] = {
     "frx_split_f32": (_I32, [_P, _I64, _I64, _I64, ctypes.c_uint32, _I32, _P, _I64, _I64, _P]),
     "frx_test_stalled_fwd": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I64, _P, _P]),
     "frx_check_range": (_I32, [_P, _I64]),
+    "frx_clock_probe": (_I32, [_P, _I32, _P]),
 }
 
 _lib = None

@@ -230,6 +230,15 @@ FRX_API int frx_fwd_ce_entropy_noalloc(const void* hidden, int64_t ld_hidden, co
 FRX_API int frx_check_range(const void* ptr, int64_t bytes);
 
 /*
+ * Measurement aid: when the stream reaches it, blocks spread over the GPU write, for each SM s they
+ * land on, out[2s] = that SM's cycle counter (%clock64) and out[2s + 1] = the global timer in
+ * nanoseconds (%globaltimer); slots of SMs no block landed on are left as they were (zero them
+ * first). Two probes around a timed region give its average SM clock per SM:
+ * (c1 - c0) / (t1 - t0) GHz. `out` holds 2 * max_sms values. No counterpart in the reference.
+ */
+FRX_API int frx_clock_probe(uint64_t* out, int max_sms, void* stream);
+
+/*
  * Test hook for failure detection (not part of the computation): runs the bf16 forward of
  * frx_fwd_partials with k-block `stall_kb` of each CTA pair's first tile left unfilled on purpose, so
  * the MMA warp's bounded wait on that pipeline stage runs out after `wait_limit_us` microseconds
