@@ -184,7 +184,7 @@ static int check_out(void* out, int64_t ld, int64_t cols, int out_dtype, const c
   return FRX_OK;
 }
 
-static int64_t out_elem_bytes(int out_dtype) {
+[[maybe_unused]] static int64_t out_elem_bytes(int out_dtype) {
   return (out_dtype & ~FRX_OUT_ACCUMULATE) == FRX_DTYPE_F32 ? 4 : 2;
 }
 

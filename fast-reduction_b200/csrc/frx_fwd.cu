@@ -219,7 +219,7 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
               "frx_fwd_partials: logits must be 16-byte aligned with ld_logits a multiple of 4 (got %lld)",
               (long long)ld_logits);
   const int64_t n_tiles = (vocab_shard + kBN - 1) / kBN;
-  const int64_t esz = 2;
+  [[maybe_unused]] const int64_t esz = 2;
   FRX_CHECK_RANGE(hidden, matrix_bytes(rows, hidden_dim, ld_hidden, esz), "frx_fwd_partials: hidden");
   FRX_CHECK_RANGE(weight, matrix_bytes(vocab_shard, hidden_dim, ld_weight, esz), "frx_fwd_partials: weight");
   FRX_CHECK_RANGE(bias, vocab_shard * esz, "frx_fwd_partials: bias");

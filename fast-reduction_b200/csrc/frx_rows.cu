@@ -184,7 +184,7 @@ extern "C" int frx_logits_partials(const void* logits, int dtype, int64_t ld, in
               "frx_logits_partials: null logits/partials or unaligned partials");
   const int64_t n_tiles = (cols + tile_cols - 1) / tile_cols;
   FRX_REQUIRE(n_tiles < (1ll << 31), FRX_ERR_INVALID_ARG, "frx_logits_partials: too many tiles");
-  const int64_t esz = dtype == FRX_DTYPE_F32 ? 4 : 2;
+  [[maybe_unused]] const int64_t esz = dtype == FRX_DTYPE_F32 ? 4 : 2;
   FRX_CHECK_RANGE(logits, matrix_bytes(rows, cols, ld, esz), "frx_logits_partials: logits");
   FRX_CHECK_RANGE(target, rows * 8, "frx_logits_partials: target");
   FRX_CHECK_RANGE(partials, matrix_bytes(n_tiles, rows, tile_stride, 16), "frx_logits_partials: partials");
