@@ -426,7 +426,7 @@ def run_ours(args, world, rank, local):
 
     # ---- configs[0] (B=1024, H=1024, V=32000, chunk 512): a launch-bound size, eager vs CUDA graph
     small = None
-    if world == 1:
+    if world == 1 and not args.no_config0:
         from fast_reduction.graphs import graphed_forward
 
         g0 = torch.Generator().manual_seed(0)
@@ -667,6 +667,7 @@ def main():
     ap.add_argument("--no-fwd-bwd", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config0", action="store_true", help="skip the configs[0] eager-vs-graph line")
     ap.add_argument("--micro", action="store_true", help="time the HBM-bound kernels alone (one line each)")
     ap.add_argument("--micro-scale", type=int, default=1, help="divide the --micro row counts (small ncu cases)")
     args = ap.parse_args()
