@@ -8,7 +8,8 @@ The same line also reports the training step (`gemm_megakernel_fast` + loss.back
 under "fwd_bwd".
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-    python bench.py --micro        (HBM-bound kernels alone: finalize, dlogits, column sums, CE over logits)
+    python bench.py --micro        (HBM-bound kernels alone: finalize, dlogits, column sums, fp32 split,
+                                    CE over logits)
     torchrun --nproc-per-node N bench.py --gpus N ...      (vocabulary sharded over N GPUs)
 
 Timing: CUDA events on the launching stream, barrier + synchronize on both sides, max over ranks.
@@ -643,6 +644,14 @@ def run_micro(args):
     ms = timeit(lambda: ops.column_sums(big, db, rows=R2, cols=V), iters=5)
     report("column_sums", [R2, V], ms, R2 * V * 2 + V * 4, "2 B per element read + 4 B per column written")
     del big, dz
+
+    # fp32 -> bf16 hi / mid / lo parts (the fp32 input path's split), a [32768, 4096] hidden
+    R4, C4 = 32768 // sc, 4096
+    xf = torch.randn(R4, C4, device=dev, generator=g)
+    parts = torch.empty(3, R4, C4, device=dev, dtype=torch.bfloat16)
+    ms = timeit(lambda: ops.split_f32(xf, parts[0], (0, 1, 2), part_stride=R4 * C4))
+    report("split_f32", [R4, C4], ms, R4 * C4 * (4 + 3 * 2), "4 B fp32 read + three 2 B parts written per element")
+    del xf, parts
 
     # standalone CE / entropy over materialised bf16 logits [32768, 32000] (configs[0]'s vocabulary).
     M3, N3 = 32768 // sc, 32000
