@@ -51,3 +51,24 @@ def test_parity_suites_pass_under_the_checked_build():
     out = subprocess.run([sys.executable, "-m", "pytest", *suites, "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider"],
                          cwd=REPO, env=env, capture_output=True, text=True, timeout=1200)
     assert out.returncode == 0, (out.stdout[-3000:], out.stderr[-2000:])
+
+
+def test_clock_probe_reads_a_plausible_sm_clock():
+    """frx_clock_probe stamps every SM; two probes around GPU work give that work's SM clock."""
+    from fast_reduction import _native as nat
+
+    lib = nat.load()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    buf = torch.zeros(2, 2 * 256, dtype=torch.int64, device="cuda")
+    stream = nat.stream_of(buf.device)
+    assert lib.frx_clock_probe(buf[0].data_ptr(), 256, stream) == nat.FRX_OK
+    a = torch.randn(4096, 4096, device="cuda")
+    for _ in range(20):
+        a = a @ a * 1e-3
+    assert lib.frx_clock_probe(buf[1].data_ptr(), 256, stream) == nat.FRX_OK
+    b = buf.cpu().view(2, 256, 2)
+    stamped = [s for s in range(256) if b[0, s, 1] and b[1, s, 1]]
+    assert len(stamped) >= sms // 2
+    mhz = sorted(float(b[1, s, 0] - b[0, s, 0]) / float(b[1, s, 1] - b[0, s, 1]) * 1000 for s in stamped)
+    assert 300 < mhz[len(mhz) // 2] < 2500
+    assert lib.frx_clock_probe(buf[0].data_ptr(), 0, stream) == nat.FRX_ERR_INVALID_ARG
