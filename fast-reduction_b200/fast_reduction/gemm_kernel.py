@@ -210,6 +210,14 @@ def forward_stats(
 _HOST_SLICE_TILES = 32
 # Bound on the [tiles, rows, 4] fp32 partials buffer of the host-streamed path.
 _HOST_PARTIALS_BYTES = 1 << 30
+# When hidden and weight are both on the host, this many weight rows (the "head") go up first and
+# the hidden follows in chunks of _HOST_HIDDEN_CHUNK rows; each chunk's GEMM against the head runs
+# while the next chunk is in flight. The head is sized so that those GEMMs last about as long as the
+# chunk uploads: rows*head*H*2 FLOP at the tensor rate F equals rows*H*2 bytes at the PCIe rate P
+# when head = F / P, about 1.5e15 / 57e9 = 26,000 rows for 16-bit operands on a B200 (independent of
+# rows and H). Without a head the tensor cores wait for the whole hidden before the first GEMM.
+_HOST_HEAD_VOCAB = 96 * 256
+_HOST_HIDDEN_CHUNK = 2048
 _copy_streams: dict = {}
 
 
@@ -232,6 +240,28 @@ def _to_device(t: Optional[Tensor], dev: torch.device, stream: torch.cuda.Stream
     return out
 
 
+def _upload_rows(src: Tensor, dst: Optional[Tensor], dev: torch.device, bounds, stream: torch.cuda.Stream):
+    """Enqueues on `stream` the copy of src[a:b] into a device buffer for each (a, b) in `bounds`
+    (none when `src` is already on `dev`); returns (buffer, [(a, b, event after that copy)])."""
+    if src.device == dev:
+        buf, out = src, []
+        with torch.cuda.stream(stream):
+            for a, b in bounds:
+                ev = torch.cuda.Event()
+                ev.record(stream)
+                out.append((a, b, ev))
+        return buf, out
+    buf = torch.empty(src.shape, dtype=src.dtype, device=dev) if dst is None else dst
+    out = []
+    with torch.cuda.stream(stream):
+        for a, b in bounds:
+            buf[a:b].copy_(src[a:b], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            out.append((a, b, ev))
+    return buf, out
+
+
 def forward_stats_from_host(
     hidden_2d: Tensor,
     weight: Tensor,
@@ -251,12 +281,16 @@ def forward_stats_from_host(
 ) -> None:
     """forward_stats when some inputs are host (CPU) tensors: the uploads overlap the GEMMs.
 
-    On a copy stream: target, bias and hidden (whichever are on the host), then the weight in slices
-    of _HOST_SLICE_TILES vocabulary tiles. The current stream launches one GEMM-epilogue per weight
-    slice over all rows of a row group as soon as that slice is resident; each launch writes the
-    partials of its own vocabulary tiles, so the result equals the device-resident path bit for bit
-    (the same tiles, each reduced in the same order). Outputs are device tensors given by the caller.
-    Host inputs should be pinned for the copies to overlap; pageable memory is correct but serialises.
+    On a copy stream: target and bias (whichever are on the host), then hidden and weight. The
+    weight goes up in slices of _HOST_SLICE_TILES vocabulary tiles; when hidden and weight are both
+    on the host (and the partials of all rows fit in one buffer) the first _HOST_HEAD_VOCAB weight
+    rows go first and the hidden follows in _HOST_HIDDEN_CHUNK-row chunks. The current stream
+    launches one GEMM-epilogue per (hidden chunk, head) as each chunk lands, then one per remaining
+    weight slice over all rows of a row group. Each launch writes the partials of its own rows and
+    vocabulary tiles, and a row's partials over a tile do not depend on how rows are grouped, so the
+    result equals the device-resident path bit for bit (the same tiles, each reduced in the same
+    order). Outputs are device tensors given by the caller. Host inputs should be pinned for the
+    copies to overlap; pageable memory is correct but serialises.
 
     ``hidden_share = (rank, world, gather)`` splits the upload of a host ``hidden_2d`` over ranks that
     all hold the same rows: this rank uploads only rows [rank*c, (rank+1)*c) of c = ceil(B/world) into
@@ -271,8 +305,21 @@ def forward_stats_from_host(
     cp = _copy_stream(dev)
     # Device buffers come from the current stream's pool: copies into them start after its prior work.
     cp.wait_stream(cur)
-    share_ev = None
-    if hidden_share is not None and hidden_2d.device != dev:
+    T = ops.n_vocab_tiles(V)
+    group = max(ops.VOCAB_TILE, _HOST_PARTIALS_BYTES // (16 * T) // ops.VOCAB_TILE * ops.VOCAB_TILE)
+    group = min(group, B)
+    vocab_size = V if vocab_size is None else vocab_size
+    t_d = _to_device(target_1d, dev, cp)
+    b_d = _to_device(bias, dev, cp)
+    w_host = weight.device != dev
+    h_host = hidden_2d.device != dev
+    head = 0
+    if w_host and h_host and hidden_share is None and group == B:
+        head = min(V, max(ops.VOCAB_TILE, _HOST_HEAD_VOCAB // ops.VOCAB_TILE * ops.VOCAB_TILE))
+    step = _HOST_SLICE_TILES * ops.VOCAB_TILE if w_host else V
+    w_d, head_slices = _upload_rows(weight, None, dev, [(0, head)] if head else [], cp)
+    share_ev, h_chunks = None, []
+    if hidden_share is not None and h_host:
         rank, world, gather = hidden_share
         c = (B + world - 1) // world
         lo, hi = min(B, rank * c), min(B, (rank + 1) * c)
@@ -283,33 +330,27 @@ def forward_stats_from_host(
             share_ev = torch.cuda.Event()
             share_ev.record(cp)
         h_d = None
+    elif head:
+        chunk = max(1, _HOST_HIDDEN_CHUNK)
+        h_d, h_chunks = _upload_rows(hidden_2d, None, dev, [(a, min(a + chunk, B)) for a in range(0, B, chunk)], cp)
     else:
         h_d = _to_device(hidden_2d, dev, cp)
-    t_d = _to_device(target_1d, dev, cp)
-    b_d = _to_device(bias, dev, cp)
-    # slices: (first row, end row, event after which the slice and every earlier upload are resident)
-    slices = []
-    step = V if weight.device == dev else _HOST_SLICE_TILES * ops.VOCAB_TILE
-    w_d = weight if weight.device == dev else torch.empty(weight.shape, dtype=weight.dtype, device=dev)
-    with torch.cuda.stream(cp):
-        for a in range(0, V, step):
-            b = min(a + step, V)
-            if w_d is not weight:
-                w_d[a:b].copy_(weight[a:b], non_blocking=True)
-            ev = torch.cuda.Event()
-            ev.record(cp)
-            slices.append((a, b, ev))
+    # rest: (first row, end row, event after which the slice and every earlier upload are resident)
+    w_d, rest = _upload_rows(weight, w_d if w_host else None, dev,
+                             [(a, min(a + step, V)) for a in range(head, V, step)], cp)
     if share_ev is not None:
         cur.wait_event(share_ev)
         h_d = gather(share)[:B]
-    T = ops.n_vocab_tiles(V)
-    group = max(ops.VOCAB_TILE, _HOST_PARTIALS_BYTES // (16 * T) // ops.VOCAB_TILE * ops.VOCAB_TILE)
-    group = min(group, B)
     partials = torch.empty(T, group, 4, device=dev, dtype=torch.float32)
-    vocab_size = V if vocab_size is None else vocab_size
+    flat = partials.view(-1)
+    for r0, r1, ev in h_chunks:
+        # the head was enqueued before every hidden chunk, so this event covers it too
+        cur.wait_event(ev)
+        ops.fwd_partials(h_d[r0:r1], w_d[:head], t_d[r0:r1], flat[4 * r0:], group, vocab_offset,
+                         bias=None if b_d is None else b_d[:head])
     for start in range(0, B, group):
         end = min(start + group, B)
-        for a, b, ev in slices:
+        for a, b, ev in rest:
             if start == 0:
                 cur.wait_event(ev)
             ops.fwd_partials(h_d[start:end], w_d[a:b], t_d[start:end], partials[a // ops.VOCAB_TILE:], group,

@@ -137,7 +137,7 @@ def fwd_partials(
         raise ValueError("target must be a contiguous int64 tensor with one id per row")
     if partials.dtype != torch.float32 or not partials.is_contiguous():
         raise ValueError("partials must be contiguous float32")
-    if partials.numel() < 4 * n_vocab_tiles(vshard) * tile_stride:
+    if tile_stride < rows or partials.numel() < 4 * ((n_vocab_tiles(vshard) - 1) * tile_stride + rows):
         raise ValueError("partials buffer too small")
     if bias is not None and (bias.dtype != hidden.dtype or not bias.is_contiguous() or bias.numel() != vshard):
         raise ValueError("bias must be a contiguous tensor of the weight's dtype with one value per vocabulary row "

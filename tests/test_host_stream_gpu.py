@@ -1,5 +1,6 @@
-"""GPU: the forward over host (CPU) inputs — weight uploaded in slices under the GEMMs, rows in
-groups bounded by the partials buffer — returns exactly what the device-resident forward returns."""
+"""GPU: the forward over host (CPU) inputs — weight uploaded in slices under the GEMMs, a head of the
+weight ahead of a chunked hidden upload, rows in groups bounded by the partials buffer — returns
+exactly what the device-resident forward returns."""
 
 import pytest
 import torch
@@ -33,6 +34,26 @@ def test_host_inputs_match_device_path(small_slices, pinned, with_bias):
     for a, b in zip(out, ref):
         assert a.device.type == "cpu" and a.shape == b.shape
         assert torch.equal(a, b.cpu())
+
+
+@pytest.mark.parametrize("head_tiles", [3, 64], ids=["head-3-tiles", "head-covers-weight"])
+@pytest.mark.parametrize("with_bias", [False, True], ids=["no-bias", "bias"])
+def test_head_first_schedule_matches_device_path(monkeypatch, head_tiles, with_bias):
+    """Hidden and weight both on the host: a head of the weight goes up first, the hidden follows in
+    256-row chunks (the last one ragged) whose GEMMs against the head write partials at row offsets,
+    then 2-tile slices over all rows. With 64 head tiles the head is the whole (12-tile) weight."""
+    monkeypatch.setattr(gk, "_HOST_SLICE_TILES", 2)
+    monkeypatch.setattr(gk, "_HOST_HEAD_VOCAB", head_tiles * 256)
+    monkeypatch.setattr(gk, "_HOST_HIDDEN_CHUNK", 256)
+    B, H, V = 700, 256, 3001
+    h, w, t = rm.make_inputs(B, H, V, seed=14, weight_std=0.1, ignore_frac=0.05, tail_frac=0.02)
+    bias = (torch.randn(V, generator=torch.Generator().manual_seed(4)) * 0.5).to(torch.bfloat16) if with_bias else None
+    dev = torch.device("cuda", 0)
+    ref = gk.gemm_fused_ce_entropy(h.to(dev), w.to(dev), t.to(dev), bias=None if bias is None else bias.to(dev))
+    out = gk.gemm_fused_ce_entropy(h.pin_memory(), w.pin_memory(), t.pin_memory(),
+                                   bias=None if bias is None else bias.pin_memory())
+    for a, b in zip(out, ref):
+        assert a.device.type == "cpu" and torch.equal(a, b.cpu())
 
 
 def test_host_weight_device_hidden(small_slices):
