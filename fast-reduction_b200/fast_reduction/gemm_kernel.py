@@ -206,8 +206,11 @@ def forward_stats(
 
 
 # Host-resident inputs (forward_stats_from_host): the weight is uploaded in slices of this many
-# 256-row vocabulary tiles, so the GEMM over one slice runs while the next is in flight.
+# 256-row vocabulary tiles, so the GEMM over one slice runs while the next is in flight. The first
+# slices are smaller (_HOST_FIRST_SLICE_TILES, doubling up to _HOST_SLICE_TILES) so the first GEMM
+# after the hidden is resident waits for less weight.
 _HOST_SLICE_TILES = 32
+_HOST_FIRST_SLICE_TILES = 4
 # Bound on the [tiles, rows, 4] fp32 partials buffer of the host-streamed path.
 _HOST_PARTIALS_BYTES = 1 << 30
 # When hidden and weight are both on the host, this many weight rows (the "head") go up first and
@@ -282,7 +285,7 @@ def forward_stats_from_host(
     """forward_stats when some inputs are host (CPU) tensors: the uploads overlap the GEMMs.
 
     On a copy stream: target and bias (whichever are on the host), then hidden and weight. The
-    weight goes up in slices of _HOST_SLICE_TILES vocabulary tiles; when hidden and weight are both
+    weight goes up in slices of up to _HOST_SLICE_TILES vocabulary tiles; when hidden and weight are both
     on the host (and the partials of all rows fit in one buffer) the first _HOST_HEAD_VOCAB weight
     rows go first and the hidden follows in _HOST_HIDDEN_CHUNK-row chunks. The current stream
     launches one GEMM-epilogue per (hidden chunk, head) as each chunk lands, then one per remaining
@@ -316,8 +319,13 @@ def forward_stats_from_host(
     head = 0
     if w_host and h_host and hidden_share is None and group == B:
         head = min(V, max(ops.VOCAB_TILE, _HOST_HEAD_VOCAB // ops.VOCAB_TILE * ops.VOCAB_TILE))
-    step = _HOST_SLICE_TILES * ops.VOCAB_TILE if w_host else V
-    w_d, head_slices = _upload_rows(weight, None, dev, [(0, head)] if head else [], cp)
+    bounds = [(head, V)] if head < V else []
+    if w_host:
+        bounds, a, tiles = [], head, max(1, min(_HOST_FIRST_SLICE_TILES, _HOST_SLICE_TILES))
+        while a < V:
+            bounds.append((a, min(a + tiles * ops.VOCAB_TILE, V)))
+            a, tiles = bounds[-1][1], min(2 * tiles, _HOST_SLICE_TILES)
+    w_d, _ = _upload_rows(weight, None, dev, [(0, head)] if head else [], cp)
     share_ev, h_chunks = None, []
     if hidden_share is not None and h_host:
         rank, world, gather = hidden_share
@@ -336,8 +344,7 @@ def forward_stats_from_host(
     else:
         h_d = _to_device(hidden_2d, dev, cp)
     # rest: (first row, end row, event after which the slice and every earlier upload are resident)
-    w_d, rest = _upload_rows(weight, w_d if w_host else None, dev,
-                             [(a, min(a + step, V)) for a in range(head, V, step)], cp)
+    w_d, rest = _upload_rows(weight, w_d if w_host else None, dev, bounds, cp)
     if share_ev is not None:
         cur.wait_event(share_ev)
         h_d = gather(share)[:B]
