@@ -174,9 +174,12 @@ int main(void) {
     check("lse", r, g_lse[r], lse, 1e-4 + 1e-5 * fabs(lse));
     check("entropy", r, g_ent[r], ent, 1e-4 + 1e-5 * fabs(ent));
     check("ce", r, g_ce[r], ce, 1e-4 + 1e-5 * fabs(ce));
-    for (int64_t j = 0; j < V; ++j) { /* dz = p (1 + (log p + H)) - [j == t], ce_weight 1, ent_weight -1 */
+    /* dz = p (g_ce + (log p + H)) - g_ce [j == t] with ent_weight -1; g_ce = 1, or 0 on an ignored
+       row, which (nll_loss semantics) drops the whole CE term and keeps the entropy term */
+    const double g_ce = h_t[r] == IGNORE ? 0.0 : 1.0;
+    for (int64_t j = 0; j < V; ++j) {
       double lp = z[j] - lse, p = exp(lp);
-      dz[j] = p * (1.0 + (lp + ent)) - (j == h_t[r] ? 1.0 : 0.0);
+      dz[j] = p * (g_ce + (lp + ent)) - (j == h_t[r] ? g_ce : 0.0);
       double got = from_bf16(g_dz[r * V + j]);
       /* bf16 keeps 8 significant bits (half an ulp is 2^-9 relative); the fp32 logits and lse add
          ~1e-6 absolute to log p, i.e. ~1e-6 p to dz, which dominates where 1 + log p + H cancels */
