@@ -97,6 +97,41 @@ def test_invalid_arguments_return_codes_without_gpu():
     assert rc == nat.FRX_ERR_INVALID_ARG  # wait limit must be positive
 
 
+def test_last_error_is_per_thread():
+    """frx_last_error() reports the last failure of the calling thread only (ctypes releases the
+    GIL around each call, so the two threads' calls interleave for real)."""
+    import threading
+
+    from fast_reduction import _native as nat
+
+    lib = nat.load()
+    step = threading.Barrier(2, timeout=30)
+    seen = {}
+
+    def a():
+        lib.frx_fwd_partials(None, 0, None, 0, 0, None, None, -1, 10, 64, 0, None, 0, None, 0, None, None)
+        step.wait()  # 1: A has failed
+        step.wait()  # 2: B has failed
+        seen["a"] = lib.frx_last_error()
+
+    def b():
+        step.wait()
+        seen["b_before"] = lib.frx_last_error()
+        lib.frx_fwd_partials(1 << 20, 64, 1 << 21, 64, nat.FRX_DTYPE_F32, None, None, 8, 10, 64, 0, 1 << 22, 8,
+                             None, 0, None, None)
+        seen["b"] = lib.frx_last_error()
+        step.wait()
+
+    threads = [threading.Thread(target=a), threading.Thread(target=b)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(60)
+    assert b"bad sizes" in seen["a"] and b"dtype" not in seen["a"]
+    assert seen["b_before"] == b""
+    assert b"dtype" in seen["b"] and b"bad sizes" not in seen["b"]
+
+
 def test_empty_problems_are_noops():
     from fast_reduction import _native as nat
 
