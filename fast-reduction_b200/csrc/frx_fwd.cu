@@ -246,10 +246,12 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
   ep.tile_stride = tile_stride;
   Operand a{hidden, ld_hidden, rows, hidden_dim, false, dtype};
   Operand b{weight, ld_weight, vocab_shard, hidden_dim, false, dtype};
-  // A band of up to 64 row blocks (8192 rows, 64 MiB of bf16 hidden at H=4096) stays in L2
-  // while the CTAs sweep the vocabulary.
+  // A band of up to 32 row blocks (4096 rows, 32 MiB of bf16 hidden at H=4096) stays in L2
+  // while the CTAs sweep the vocabulary. Measured on one B200 at vocabulary shards of 16032 to
+  // 128256 rows: 4096-row bands beat 8192- and 16384-row bands everywhere (e.g. 2.64 / 2.93 /
+  // 3.25 ms over 32768 rows at 16032), and 2048-row bands lose at 128256.
   // FRX_FWD_GROUP_M (tuning only) overrides the band height in 128-row blocks.
-  static const int group_m = env_int("FRX_FWD_GROUP_M", 64);
+  static const int group_m = env_int("FRX_FWD_GROUP_M", 32);
   return launch_gemm<false, false, false, CEPartialsEpilogue>(a, b, rows, vocab_shard, hidden_dim, group_m, ep, status,
                                                               static_cast<cudaStream_t>(stream), stall_kb,
                                                               wait_limit_ns);

@@ -159,6 +159,20 @@ def _fp32_parts(x: Tensor) -> Tensor:
     return out[:, :, :cols]
 
 
+# The forward launches chunk_size rows at a time, or a multiple of it while the partials of one
+# launch ([tiles, rows, 4] fp32) stay within this many bytes. Small vocabulary shards then run as
+# one launch over many rows: one pipeline fill and one tail instead of several, and fewer partial
+# waves. Measured on one B200 over 32768 rows (4096-row bands): shard 16032 (8 GPUs) 2.74-2.79 ms
+# in 4096-row launches vs 2.64 ms in one launch; shard 32064 5.77 vs 5.66 ms; shard 64128 and the
+# full 128256 vocabulary unchanged within noise (the full vocabulary keeps 4096-row launches).
+_FWD_LAUNCH_PARTIALS_BYTES = 48 << 20
+
+
+def _launch_rows(chunk: int, B: int, n_tiles: int) -> int:
+    k = max(1, _FWD_LAUNCH_PARTIALS_BYTES // (16 * max(1, n_tiles) * chunk))
+    return min(B, chunk * k)
+
+
 def forward_stats(
     hidden_2d: Tensor,
     weight: Tensor,
@@ -178,14 +192,15 @@ def forward_stats(
     """Forward over one vocabulary shard, chunked over rows: GEMM-epilogue partials + finalize.
 
     Writes whichever of ce / entropy / lse / log_probs / merged ([B, 4] (M, S, U, ZT) per row,
-    for a later cross-shard merge) are given.
+    for a later cross-shard merge) are given. Rows go in launches of chunk_size rows or a multiple
+    of it (_launch_rows); a row's results do not depend on how rows are grouped.
     """
     B = hidden_2d.shape[0]
     V = weight.shape[0]
     if B == 0:
         return
     T = ops.n_vocab_tiles(V)
-    chunk = _chunk_rows(chunk_size, B)
+    chunk = _launch_rows(_chunk_rows(chunk_size, B), B, T)
     partials = torch.empty(T, chunk, 4, device=hidden_2d.device, dtype=torch.float32)
     vocab_size = V if vocab_size is None else vocab_size
     for start in range(0, B, chunk):

@@ -140,17 +140,25 @@ def test_config0_parity_vs_fp32_and_reference_chunked():
     assert (ent - ref_ent).abs().mean() <= 2e-4
 
 
-def test_chunking_is_bit_invariant_and_deterministic():
+def test_chunking_is_bit_invariant_and_deterministic(monkeypatch):
+    from fast_reduction import gemm_kernel as gk
     from fast_reduction.gemm_kernel import gemm_fused_ce_entropy
 
     h, w, t = rm.make_inputs(1000, 256, 5000, seed=11, weight_std=0.1)
     hd, wd, td = h.to(DEV), w.to(DEV), t.to(DEV)
     a = gemm_fused_ce_entropy(hd, wd, td, chunk_size=1000)
+    # small shards merge chunks into one launch: a budget of 0 keeps one launch per 96-row chunk
+    monkeypatch.setattr(gk, "_FWD_LAUNCH_PARTIALS_BYTES", 0)
     b = gemm_fused_ce_entropy(hd, wd, td, chunk_size=96)
-    c = gemm_fused_ce_entropy(hd, wd, td, chunk_size=1000)
-    for x, y, z in zip(a, b, c):
+    # 3 chunks per launch (the last launch ragged)
+    monkeypatch.setattr(gk, "_FWD_LAUNCH_PARTIALS_BYTES", 16 * 20 * 96 * 3)
+    c = gemm_fused_ce_entropy(hd, wd, td, chunk_size=96)
+    monkeypatch.undo()
+    d = gemm_fused_ce_entropy(hd, wd, td, chunk_size=1000)
+    for x, y, z, u in zip(a, b, c, d):
         assert torch.equal(x, y)
         assert torch.equal(x, z)
+        assert torch.equal(x, u)
 
 
 def test_ignore_index_and_batch_shapes():

@@ -91,6 +91,19 @@ def test_tile_helpers():
     assert ops.round_up(1000, 8) == 1000 and ops.round_up(1001, 8) == 1008
 
 
+def test_forward_launch_rows():
+    """Rows per forward launch: chunk_size, or a multiple of it while one launch's partials stay
+    within _FWD_LAUNCH_PARTIALS_BYTES (48 MiB)."""
+    T = ops.n_vocab_tiles
+    assert gk._launch_rows(4096, 32768, T(128256)) == 4096      # full vocabulary: as given
+    assert gk._launch_rows(4096, 32768, T(64128)) == 12288      # 2 GPUs: 3 chunks per launch
+    assert gk._launch_rows(4096, 32768, T(32064)) == 24576      # 4 GPUs: 6 chunks per launch
+    assert gk._launch_rows(4096, 32768, T(16032)) == 32768      # 8 GPUs: one launch
+    assert gk._launch_rows(512, 1024, T(32000)) == 1024
+    assert gk._launch_rows(300, 200, T(1000)) == 200
+    assert gk._launch_rows(4096, 65536, T(1 << 24)) == 4096     # partials of one chunk exceed the budget
+
+
 def test_lazy_exports():
     import fast_reduction
 
