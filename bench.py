@@ -404,8 +404,11 @@ def run_ours(args, world, rank, local):
     flops_fwd = 2.0 * B * H * V
     gemm = ksum.get("fwd_partials", {"launches": 1, "total_ms": float("nan")})
     gemm_avg_ms = gemm["total_ms"] / max(gemm["launches"], 1)
-    rows_per_launch = min(chunk, B)
-    gemm_flops = 2.0 * rows_per_launch * Vr * H
+    # The forward launches chunk-size row groups, merged while a launch's partials stay small
+    # (gemm_kernel._launch_rows): count the launches of a step rather than assume one per chunk.
+    launches_per_step = max(gemm["launches"] / args.steps, 1.0)
+    rows_per_launch = int(round(B / launches_per_step))
+    gemm_flops = 2.0 * B * Vr * H / launches_per_step
     achieved_tflops = gemm_flops / (gemm_avg_ms / 1000.0) / 1e12
     peak_tf = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     peak_sus = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
