@@ -97,6 +97,22 @@ def test_invalid_arguments_return_codes_without_gpu():
     assert rc == nat.FRX_ERR_INVALID_ARG  # wait limit must be positive
 
 
+def test_integration_stub_matches_the_bindings():
+    """The ctypes stub INTEGRATION.md shows a maintainer declares the same argument types as the
+    package's own binding (fast_reduction/_native.py) for every entry point it lists."""
+    from fast_reduction import _native as nat
+
+    names = {"P": ctypes.c_void_p, "I64": ctypes.c_int64, "I32": ctypes.c_int, "F32": ctypes.c_float,
+             "ctypes.c_uint32": ctypes.c_uint32}
+    text = (REPO / "INTEGRATION.md").read_text()
+    stubs = re.findall(r"^_lib\.(frx_\w+)\.argtypes = \[([^\]]*)\]", text, flags=re.M)
+    assert len(stubs) >= 9
+    for fn, args in stubs:
+        declared = [names[a.strip()] for a in args.split(",")]
+        assert fn in nat.SIGNATURES, fn
+        assert declared == list(nat.SIGNATURES[fn][1]), fn
+
+
 def test_last_error_is_per_thread():
     """frx_last_error() reports the last failure of the calling thread only (ctypes releases the
     GIL around each call, so the two threads' calls interleave for real)."""
