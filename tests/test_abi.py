@@ -5,7 +5,6 @@ import ctypes
 import re
 from pathlib import Path
 
-import pytest
 
 REPO = Path(__file__).resolve().parents[1]
 HEADER = REPO / "include" / "frx.h"

@@ -2,7 +2,6 @@
 fp32 ground truth. Shapes and seeds follow the reference's own tests (tests/test_ce_impls.py) plus
 the ragged / ignore_index / sharding cases the reference lacks."""
 
-import math
 
 import numpy as np
 import pytest

@@ -2,7 +2,6 @@
 running the reference's fast_reduction/baseline.py, tests/golden/make_golden.py) and against the
 reference's finalize known-answer construction (reference tests/test_ce_impls.py:101-138)."""
 
-import math
 from pathlib import Path
 
 import numpy as np

@@ -7,7 +7,6 @@ Also checks the slice bounds, the d_hidden all-reduce, and that a failing rank s
 error on the other ranks instead of a hang.
 """
 
-import os
 import socket
 import traceback
 
@@ -35,8 +34,6 @@ def _init(rank, world, port, timeout_s=30):
 
 def _protocol_worker(rank, world, port, q):
     try:
-        import sys
-
         from fast_reduction.vocab_parallel import shard_bounds
 
         _init(rank, world, port)
