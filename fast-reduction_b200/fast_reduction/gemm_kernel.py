@@ -258,6 +258,30 @@ def _to_device(t: Optional[Tensor], dev: torch.device, stream: torch.cuda.Stream
     return out
 
 
+def _host_upload_plan(B: int, V: int, *, w_host: bool, h_host: bool, shared_hidden: bool, one_group: bool):
+    """Upload schedule of forward_stats_from_host: (head, hidden chunks, weight slices).
+
+    head: weight rows [0, head) uploaded before the hidden (0: none); hidden chunks: row ranges
+    uploaded one by one after the head, each followed by its GEMM against the head (empty: the
+    hidden goes up whole); weight slices: row ranges [head, V) uploaded after the hidden, each
+    followed by its GEMM over all rows. A head needs both operands on the host, a hidden that is not
+    split across ranks, and the partials of all rows in one buffer."""
+    tile = ops.VOCAB_TILE
+    head = 0
+    if w_host and h_host and not shared_hidden and one_group:
+        head = min(V, max(tile, _HOST_HEAD_VOCAB // tile * tile))
+    if w_host:
+        slices, a, tiles = [], head, max(1, min(_HOST_FIRST_SLICE_TILES, _HOST_SLICE_TILES))
+        while a < V:
+            slices.append((a, min(a + tiles * tile, V)))
+            a, tiles = slices[-1][1], min(2 * tiles, _HOST_SLICE_TILES)
+    else:
+        slices = [(0, V)] if V > 0 else []
+    chunk = max(1, _HOST_HIDDEN_CHUNK)
+    chunks = [(a, min(a + chunk, B)) for a in range(0, B, chunk)] if head else []
+    return head, chunks, slices
+
+
 def _upload_rows(src: Tensor, dst: Optional[Tensor], dev: torch.device, bounds, stream: torch.cuda.Stream):
     """Enqueues on `stream` the copy of src[a:b] into a device buffer for each (a, b) in `bounds`
     (none when `src` is already on `dev`); returns (buffer, [(a, b, event after that copy)])."""
@@ -331,15 +355,8 @@ def forward_stats_from_host(
     b_d = _to_device(bias, dev, cp)
     w_host = weight.device != dev
     h_host = hidden_2d.device != dev
-    head = 0
-    if w_host and h_host and hidden_share is None and group == B:
-        head = min(V, max(ops.VOCAB_TILE, _HOST_HEAD_VOCAB // ops.VOCAB_TILE * ops.VOCAB_TILE))
-    bounds = [(head, V)] if head < V else []
-    if w_host:
-        bounds, a, tiles = [], head, max(1, min(_HOST_FIRST_SLICE_TILES, _HOST_SLICE_TILES))
-        while a < V:
-            bounds.append((a, min(a + tiles * ops.VOCAB_TILE, V)))
-            a, tiles = bounds[-1][1], min(2 * tiles, _HOST_SLICE_TILES)
+    head, chunk_bounds, bounds = _host_upload_plan(B, V, w_host=w_host, h_host=h_host,
+                                                   shared_hidden=hidden_share is not None, one_group=group == B)
     w_d, _ = _upload_rows(weight, None, dev, [(0, head)] if head else [], cp)
     share_ev, h_chunks = None, []
     if hidden_share is not None and h_host:
@@ -354,8 +371,7 @@ def forward_stats_from_host(
             share_ev.record(cp)
         h_d = None
     elif head:
-        chunk = max(1, _HOST_HIDDEN_CHUNK)
-        h_d, h_chunks = _upload_rows(hidden_2d, None, dev, [(a, min(a + chunk, B)) for a in range(0, B, chunk)], cp)
+        h_d, h_chunks = _upload_rows(hidden_2d, None, dev, chunk_bounds, cp)
     else:
         h_d = _to_device(hidden_2d, dev, cp)
     # rest: (first row, end row, event after which the slice and every earlier upload are resident)

@@ -104,6 +104,40 @@ def test_forward_launch_rows():
     assert gk._launch_rows(4096, 65536, T(1 << 24)) == 4096     # partials of one chunk exceed the budget
 
 
+def test_host_upload_plan():
+    """Upload schedule of the host-streamed forward (no GPU needed): a weight head before the hidden
+    when both are on the host, hidden chunks only with a head, and weight slices that start small,
+    double up to the slice size and tile [head, V) without gaps."""
+    tile = ops.VOCAB_TILE
+
+    def check_slices(slices, start, V):
+        assert slices[0][0] == start and slices[-1][1] == V
+        assert all(a < b for a, b in slices)
+        assert all(x[1] == y[0] for x, y in zip(slices, slices[1:]))
+        assert all(a % tile == 0 for a, _ in slices)
+
+    head, chunks, slices = gk._host_upload_plan(32768, 128256, w_host=True, h_host=True, shared_hidden=False,
+                                                one_group=True)
+    assert head == gk._HOST_HEAD_VOCAB == 24576
+    assert chunks == [(a, a + 2048) for a in range(0, 32768, 2048)]
+    check_slices(slices, head, 128256)
+    sizes = [(b - a) // tile for a, b in slices]
+    assert sizes[:4] == [4, 8, 16, 32] and max(sizes) == gk._HOST_SLICE_TILES
+    # no head: hidden split over ranks, hidden already on the device, or several partials groups
+    for kw in (dict(h_host=True, shared_hidden=True, one_group=True), dict(h_host=False, shared_hidden=False,
+               one_group=True), dict(h_host=True, shared_hidden=False, one_group=False)):
+        head, chunks, slices = gk._host_upload_plan(32768, 64128, w_host=True, **kw)
+        assert head == 0 and chunks == []
+        check_slices(slices, 0, 64128)
+    # weight resident: one "slice" covering it, no head
+    assert gk._host_upload_plan(100, 5000, w_host=False, h_host=True, shared_hidden=False,
+                                one_group=True) == (0, [], [(0, 5000)])
+    # a vocabulary smaller than the head: the whole weight is the head, no slices after the hidden
+    head, chunks, slices = gk._host_upload_plan(5000, 3001, w_host=True, h_host=True, shared_hidden=False,
+                                                one_group=True)
+    assert head == 3001 and slices == [] and chunks[-1] == (4096, 5000)
+
+
 def test_lazy_exports():
     import fast_reduction
 
