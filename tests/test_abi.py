@@ -112,6 +112,26 @@ def test_integration_stub_matches_the_bindings():
         assert declared == list(nat.SIGNATURES[fn][1]), fn
 
 
+def test_integration_calls_pass_every_argument():
+    """Every `_lib.frx_*(...)` call INTEGRATION.md shows passes as many arguments as the entry point
+    takes (top-level commas of the call, nested brackets skipped)."""
+    from fast_reduction import _native as nat
+
+    text = (REPO / "INTEGRATION.md").read_text()
+    seen = 0
+    for m in re.finditer(r"_lib\.(frx_\w+)\(", text):
+        depth, commas, j = 1, 0, m.end()
+        while depth:
+            c = text[j]
+            depth += c in "([" and 1 or (-1 if c in ")]" else 0)
+            commas += c == "," and depth == 1
+            j += 1
+        n_args = 0 if text[m.end():j - 1].strip() == "" else commas + 1
+        assert n_args == len(nat.SIGNATURES[m.group(1)][1]), m.group(1)
+        seen += 1
+    assert seen >= 8
+
+
 def test_last_error_is_per_thread():
     """frx_last_error() reports the last failure of the calling thread only (ctypes releases the
     GIL around each call, so the two threads' calls interleave for real)."""
