@@ -123,8 +123,12 @@ def test_integration_calls_pass_every_argument():
         depth, commas, j = 1, 0, m.end()
         while depth:
             c = text[j]
-            depth += c in "([" and 1 or (-1 if c in ")]" else 0)
-            commas += c == "," and depth == 1
+            if c in "([":
+                depth += 1
+            elif c in ")]":
+                depth -= 1
+            elif c == "," and depth == 1:
+                commas += 1
             j += 1
         n_args = 0 if text[m.end():j - 1].strip() == "" else commas + 1
         assert n_args == len(nat.SIGNATURES[m.group(1)][1]), m.group(1)
