@@ -9,10 +9,17 @@
 // part of the library image itself.
 //
 // Limits and sharing rules:
+//   * hidden and weight must be bf16: the call passes FRX_DTYPE_BF16 to the GEMM and takes no
+//     dtype argument.
 //   * The scratch array is kFwdScratchBytes (32 MiB) per GPU; a call needs
-//     ceil(vocab_size / 256) * rows * 16 bytes of it (e.g. up to 4096 rows per call at
-//     V = 128256). Larger calls are rejected with FRX_ERR_INVALID_ARG before any GPU work.
-//   * Every GPU that loads libfrx holds the 32 MiB until the process exits.
+//     ceil(vocab_size / 256) * rows * 16 bytes of it, so at most
+//     floor(2097152 / ceil(vocab_size / 256)) rows per call (4185 at V = 128256). Larger calls
+//     are rejected with FRX_ERR_INVALID_ARG before any GPU work.
+//   * Every GPU that has the library's module loaded holds the 32 MiB until the process exits.
+//     With CUDA's lazy module loading (the default) the driver loads the module, and reserves
+//     the array, on the first call on that device (its cudaGetSymbolAddress); a caller that
+//     hands all remaining device memory to its own allocator should make one small warm-up
+//     call before doing so.
 //   * All calls on a device share the one array. Calls whose kernels overlap on the GPU (for
 //     example on two streams without ordering between them) race on it; serialise them.
 //   * The array keeps the previous call's contents. Nothing needs to start at zero: the GEMM

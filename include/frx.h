@@ -209,11 +209,15 @@ FRX_API int frx_logits_partials(const void* logits, int dtype, int64_t ld, int64
  * partials live in a 32 MiB scratch array that is part of the library image on each GPU.
  * No counterpart in the reference. For callers that cannot call cudaMalloc (a framework that
  * owns all device memory, a serving loop that must not synchronise on an allocation, a fixed
- * memory budget). Limit: ceil(vocab_size / 256) * rows * 16 bytes <= 32 MiB (e.g. at most
- * 4096 rows per call at V = 128256); larger calls return FRX_ERR_INVALID_ARG. All calls on a
- * device share the scratch, so calls that overlap on the GPU race; the first call on a device
- * looks up the scratch address and should come before any stream capture. The whole
- * vocabulary is one shard (targets are plain vocabulary ids).
+ * memory budget). hidden and weight must both be bf16 (there is no dtype argument; fp16 data
+ * would be read as bf16). Limit: ceil(vocab_size / 256) * rows * 16 bytes <= 32 MiB, i.e. at
+ * most floor(2097152 / ceil(vocab_size / 256)) rows per call (4185 at V = 128256); larger calls
+ * return FRX_ERR_INVALID_ARG before any GPU work. All calls on a device share the scratch, so
+ * calls that overlap on the GPU race. The first call on a device looks up the scratch address;
+ * under CUDA's lazy module loading that is also when the driver reserves the 32 MiB on that
+ * device, so make one small warm-up call at start-up, before handing the remaining memory to
+ * another allocator and before any stream capture. The whole vocabulary is one shard (targets
+ * are plain vocabulary ids).
  */
 FRX_API int frx_fwd_ce_entropy_noalloc(const void* hidden, int64_t ld_hidden, const void* weight,
                                        int64_t ld_weight, const int64_t* target, int64_t rows,

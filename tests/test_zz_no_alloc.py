@@ -48,7 +48,10 @@ def test_noalloc_matches_existing_path_two_calls_in_a_row():
     from fast_reduction import _native as nat
 
     lib = nat.load()
-    cases = [(1000, 256, 5000, 1), (4096, 512, 128256 // 8, 2)]  # the second call reuses stale scratch
+    # The first call fills 63 vocabulary tiles x 2048 rows of the scratch; the second (same rows,
+    # 20 tiles) lands entirely on slots that still hold the first call's partials, so a slot it
+    # failed to write would show up as a mismatch. The third changes the row count (new layout).
+    cases = [(2048, 512, 128256 // 8, 2), (2048, 256, 5000, 1), (1000, 256, 5000, 3)]
     for B, H, V, seed in cases:
         h, w, t = rm.make_inputs(B, H, V, seed=seed, weight_std=0.1, ignore_frac=0.02)
         h, w, t = h.to(DEV), w.to(DEV), t.to(DEV)
@@ -59,6 +62,10 @@ def test_noalloc_matches_existing_path_two_calls_in_a_row():
         assert int(status.item()) == 0
         for g, e in zip(got, exp):
             torch.testing.assert_close(g, e, atol=1e-6, rtol=1e-6)
+        ignored = t == -100
+        assert int(ignored.sum()) > 0
+        assert bool((got[0][ignored] == 0).all()) and bool((got[3][ignored] == 0).all())
+        assert bool(torch.isfinite(got[1]).all()) and bool(torch.isfinite(got[2]).all())
         ce32, ent32, lp32, lse32 = rm.fp32_reference(h, w, t)
         assert (got[0] - ce32).abs().mean() <= 2e-3
         assert (got[1] - ent32).abs().mean() <= 1e-4
