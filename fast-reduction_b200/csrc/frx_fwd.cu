@@ -11,6 +11,11 @@
 // Columns at or beyond the shard's vocabulary size are skipped, not sentinel-filled. An optional
 // bias (bf16 or fp16, the operands' type) is added to each column before the reductions (and
 // before the logits store).
+//
+// Two optional logits outputs feed the training pass's dlogits kernel:
+//   fp32 logits z (pass 1, 4 bytes per logit; the reference's layout), or
+//   fp16 tile-relative logits z - m (pass 2, 2 bytes per logit), where m is the tile maximum the
+//   same launch writes into the partials; the reader adds m back (frx_dlogits_tilerel).
 #include <cstring>
 
 #include "frx_host.cuh"
@@ -42,6 +47,14 @@ __device__ __forceinline__ float2 unpack2(uint32_t w, bool f16) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
 }
 
+// Two floats as one fp16x2 word (round to nearest; low half = first value, the lower column).
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  uint32_t w;
+  memcpy(&w, &h, sizeof(w));
+  return w;
+}
+
 // v[j] += bias[j] for the valid columns of a 32-column chunk (16-bit bias, fp32 add).
 __device__ __forceinline__ void add_bias32(float (&v)[32], const uint16_t* b, int lim, bool vec, bool f16) {
   if (lim >= 32 && vec) {
@@ -70,6 +83,7 @@ struct CEPartialsEpilogue {
 
   struct Params {
     CUtensorMap tm_logits;  // fp32 [rows, vocab_shard] logits, 32 x 32 boxes, 128B swizzle
+    CUtensorMap tm_rel;     // fp16 [rows, vocab_shard] tile-relative logits, 32 x 64 boxes, 128B swizzle
     const int64_t* target;
     const uint16_t* bias;  // optional [vocab_shard] bias of this shard (bf16 or fp16 bits)
     int64_t vocab_offset;
@@ -78,6 +92,7 @@ struct CEPartialsEpilogue {
     float4* partials;
     int64_t tile_stride;
     int has_logits;
+    int has_rel;
     int bias_vec;  // bias base 16-byte aligned
     int f16;       // bias is fp16 (else bf16)
     int n_tiles;   // vocabulary tiles the partials buffer holds (checked builds verify the index)
@@ -126,7 +141,14 @@ struct CEPartialsEpilogue {
         // by row % 8, which is both bank-conflict free and the TMA 128B-swizzle layout) and write it
         // with one TMA store; rows / columns outside the matrix are clipped by the TMA unit.
         const int buf = c & 1;
-        if (lane == 0) bulk_wait_group_read<1>();  // the store that last used this buffer has read it
+        // The store that last used this buffer has read it. At a tile's first chunk wait for all of
+        // them: the previous tile may have ended on either buffer (a ragged last vocabulary tile).
+        if (lane == 0) {
+          if (c == 0)
+            bulk_wait_group_read<0>();
+          else
+            bulk_wait_group_read<1>();
+        }
         __syncwarp();
         const uint32_t rowb = stage_base + static_cast<uint32_t>(buf * 4096 + lane * 128);
 #pragma unroll
@@ -158,25 +180,26 @@ struct CEPartialsEpilogue {
       __syncwarp();
       tmem_load_32cols(tacc + static_cast<uint32_t>(c * 32), v);
       if (p.bias != nullptr) add_bias32(v, p.bias + n0 + c * 32, lim, p.bias_vec != 0, p.f16 != 0);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] -= mx;  // d = z - m
+      if (p.has_rel) store_rel(p, stage, stage_base, v, c, lim, lane, row0, n0);
       if (lim >= 32) {
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          const float d0 = v[j] - mx, d1 = v[j + 1] - mx;
-          const float e0 = ex2_approx(d0 * kLog2e);
-          const float e1 = ex2_approx(d1 * kLog2e);
+          const float e0 = ex2_approx(v[j] * kLog2e);
+          const float e1 = ex2_approx(v[j + 1] * kLog2e);
           s0 += e0;
           s1 += e1;
-          u0 = fmaf(d0, e0, u0);
-          u1 = fmaf(d1, e1, u1);
+          u0 = fmaf(v[j], e0, u0);
+          u1 = fmaf(v[j + 1], e1, u1);
         }
       } else {
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           if (j < lim) {
-            const float d = v[j] - mx;
-            const float e = ex2_approx(d * kLog2e);
+            const float e = ex2_approx(v[j] * kLog2e);
             s0 += e;
-            u0 = fmaf(d, e, u0);
+            u0 = fmaf(v[j], e, u0);
           }
         }
       }
@@ -189,7 +212,47 @@ struct CEPartialsEpilogue {
   // Called once per epilogue warp after its last tile: outstanding logits stores must finish
   // before the CTA (and its staging shared memory) goes away.
   __device__ __forceinline__ static void finish(const Params& p, int lane) {
-    if (p.has_logits && lane == 0) bulk_wait_all();
+    if ((p.has_logits || p.has_rel) && lane == 0) bulk_wait_all();
+  }
+
+  // Pass-2 store of the tile-relative logits d = z - m of 32-column chunk c (this thread's row =
+  // lane): packed to fp16 into one half of a 32 x 64 staging block (row = lane, 128 bytes per row,
+  // 16-byte chunks XOR-swizzled by row % 8: bank-conflict free and the TMA 128B-swizzle layout);
+  // each completed 64-column block (or the tile's last, partial one) leaves with one TMA store.
+  // Columns past the shard's vocabulary are clipped by the TMA unit.
+  __device__ __forceinline__ static void store_rel(const Params& p, uint8_t* stage, uint32_t stage_base,
+                                                   const float (&v)[32], int c, int lim, int lane, int row0, int n0) {
+    const int blk = c >> 1;
+    const int buf = blk & 1;
+    if ((c & 1) == 0) {
+      // The store that last used this buffer has read it (at a tile's first block: every store,
+      // since the previous tile may have ended on either buffer).
+      if (lane == 0) {
+        if (blk == 0)
+          bulk_wait_group_read<0>();
+        else
+          bulk_wait_group_read<1>();
+      }
+      __syncwarp();
+    }
+    const uint32_t rowb = stage_base + static_cast<uint32_t>(buf * 4096 + lane * 128);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint32_t w0 = pack_half2(v[8 * k], v[8 * k + 1]);
+      const uint32_t w1 = pack_half2(v[8 * k + 2], v[8 * k + 3]);
+      const uint32_t w2 = pack_half2(v[8 * k + 4], v[8 * k + 5]);
+      const uint32_t w3 = pack_half2(v[8 * k + 6], v[8 * k + 7]);
+      st_shared_v4_u32(rowb + static_cast<uint32_t>((((c & 1) * 4 + k) ^ (lane & 7)) << 4), w0, w1, w2, w3);
+    }
+    if ((c & 1) == 1 || lim <= 32) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        // Evict-first, as for the fp32 logits: the dlogits pass reads them back from DRAM.
+        tma_store_2d_hint(&p.tm_rel, stage + buf * 4096, n0 + 64 * blk, row0, l2_policy_evict_first());
+        bulk_commit_group();
+      }
+    }
   }
 };
 
@@ -200,8 +263,8 @@ namespace frx {
 static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight, int dtype,
                              const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
                              int64_t hidden_dim, int64_t vocab_offset, float* partials, int64_t tile_stride,
-                             float* logits, int64_t ld_logits, int* status, void* stream, int stall_kb,
-                             uint64_t wait_limit_ns) {
+                             float* logits, int64_t ld_logits, void* zrel, int64_t ld_zrel, int* status, void* stream,
+                             int stall_kb, uint64_t wait_limit_ns) {
   FRX_REQUIRE(rows >= 0 && vocab_shard >= 1 && hidden_dim >= 1, FRX_ERR_INVALID_ARG,
               "frx_fwd_partials: bad sizes rows=%lld vocab_shard=%lld hidden_dim=%lld", (long long)rows,
               (long long)vocab_shard, (long long)hidden_dim);
@@ -223,6 +286,14 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
   FRX_REQUIRE(logits == nullptr || (ld_logits % 4 == 0 && aligned16(logits)), FRX_ERR_INVALID_ARG,
               "frx_fwd_partials: logits must be 16-byte aligned with ld_logits a multiple of 4 (got %lld)",
               (long long)ld_logits);
+  FRX_REQUIRE(logits == nullptr || zrel == nullptr, FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials: at most one of fp32 logits and tile-relative logits per launch");
+  FRX_REQUIRE(zrel == nullptr || ld_zrel >= vocab_shard, FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials_tilerel: ld_logits_rel %lld < vocab_shard %lld", (long long)ld_zrel,
+              (long long)vocab_shard);
+  FRX_REQUIRE(zrel == nullptr || (ld_zrel % 8 == 0 && aligned16(zrel)), FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials_tilerel: logits_rel must be 16-byte aligned with ld_logits_rel a multiple of 8 "
+              "(got %lld)", (long long)ld_zrel);
   const int64_t n_tiles = (vocab_shard + kBN - 1) / kBN;
   [[maybe_unused]] const int64_t esz = 2;
   FRX_CHECK_RANGE(hidden, matrix_bytes(rows, hidden_dim, ld_hidden, esz), "frx_fwd_partials: hidden");
@@ -231,6 +302,7 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
   FRX_CHECK_RANGE(target, rows * 8, "frx_fwd_partials: target");
   FRX_CHECK_RANGE(partials, matrix_bytes(n_tiles, rows, tile_stride, 16), "frx_fwd_partials: partials");
   FRX_CHECK_RANGE(logits, matrix_bytes(rows, vocab_shard, ld_logits, 4), "frx_fwd_partials: logits");
+  FRX_CHECK_RANGE(zrel, matrix_bytes(rows, vocab_shard, ld_zrel, 2), "frx_fwd_partials_tilerel: logits_rel");
   CEPartialsEpilogue::Params ep;
   memset(&ep, 0, sizeof(ep));
   ep.n_tiles = static_cast<int>(n_tiles);
@@ -239,6 +311,11 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
     const int rc = encode_f32_2d(&ep.tm_logits, logits, rows, vocab_shard, ld_logits, 32, 32);
     if (rc) return rc;
     ep.has_logits = 1;
+  }
+  if (zrel != nullptr) {
+    const int rc = encode_16bit_2d(&ep.tm_rel, true, zrel, rows, vocab_shard, ld_zrel, 32, 64);
+    if (rc) return rc;
+    ep.has_rel = 1;
   }
   ep.target = target;
   ep.bias = static_cast<const uint16_t*>(bias);
@@ -269,8 +346,20 @@ extern "C" int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const voi
                                 int64_t hidden_dim, int64_t vocab_offset, float* partials, int64_t tile_stride,
                                 float* logits, int64_t ld_logits, int* status, void* stream) {
   return frx::fwd_partials_impl(hidden, ld_hidden, weight, ld_weight, dtype, bias, target, rows, vocab_shard,
-                                hidden_dim, vocab_offset, partials, tile_stride, logits, ld_logits, status, stream, -1,
-                                frx::kWaitLimitNs);
+                                hidden_dim, vocab_offset, partials, tile_stride, logits, ld_logits, nullptr, 0, status,
+                                stream, -1, frx::kWaitLimitNs);
+}
+
+extern "C" int frx_fwd_partials_tilerel(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
+                                        int dtype, const void* bias, const int64_t* target, int64_t rows,
+                                        int64_t vocab_shard, int64_t hidden_dim, int64_t vocab_offset, float* partials,
+                                        int64_t tile_stride, void* logits_rel, int64_t ld_logits_rel, int* status,
+                                        void* stream) {
+  FRX_REQUIRE(rows == 0 || logits_rel != nullptr, FRX_ERR_INVALID_ARG,
+              "frx_fwd_partials_tilerel: null logits_rel pointer");
+  return frx::fwd_partials_impl(hidden, ld_hidden, weight, ld_weight, dtype, bias, target, rows, vocab_shard,
+                                hidden_dim, vocab_offset, partials, tile_stride, nullptr, 0, logits_rel, ld_logits_rel,
+                                status, stream, -1, frx::kWaitLimitNs);
 }
 
 extern "C" int frx_test_stalled_fwd(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
@@ -284,6 +373,6 @@ extern "C" int frx_test_stalled_fwd(const void* hidden, int64_t ld_hidden, const
               "frx_test_stalled_fwd: stall_kb %d is past the last k-block of hidden_dim %lld", stall_kb,
               (long long)hidden_dim);
   return fwd_partials_impl(hidden, ld_hidden, weight, ld_weight, FRX_DTYPE_BF16, nullptr, target, rows, vocab_shard,
-                           hidden_dim, 0, partials, tile_stride, nullptr, 0, status, stream, stall_kb,
+                           hidden_dim, 0, partials, tile_stride, nullptr, 0, nullptr, 0, status, stream, stall_kb,
                            static_cast<uint64_t>(wait_limit_us) * 1000ull);
 }

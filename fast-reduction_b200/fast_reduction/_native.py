@@ -64,6 +64,12 @@ SIGNATURES: dict[str, tuple] = {
     "frx_last_error": (ctypes.c_char_p, []),
     "frx_fwd_partials": (_I32, [_P, _I64, _P, _I64, _I32, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P, _I64, _P,
                                 _P]),
+    "frx_fwd_partials_tilerel": (_I32, [_P, _I64, _P, _I64, _I32, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _P,
+                                        _I64, _P, _P]),
+    "frx_dlogits_tilerel": (
+        _I32,
+        [_P, _I64, _P, _I64, _P, _P, _P, _P, _P, _F32, _F32, _P, _I64, _I32, _I64, _I64, _I64, _I64, _P],
+    ),
     "frx_finalize": (_I32, [_P, _I64, _I64, _I64, _I32, _P, _I64, _I64, _P, _P, _P, _P, _P, _P, _P]),
     "frx_dlogits": (
         _I32,
@@ -77,6 +83,8 @@ SIGNATURES: dict[str, tuple] = {
     "frx_gemm_dhidden_multicast": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I64, _I64, _I64, _P, _P]),
     "frx_split_f32": (_I32, [_P, _I64, _I64, _I64, ctypes.c_uint32, _I32, _P, _I64, _I64, _P]),
     "frx_test_stalled_fwd": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _P, _I64, _I32, _I64, _P, _P]),
+    "frx_loss_sum": (_I32, [_P, _P, _I64, _F32, _F32, _P, _P]),
+    "frx_scale_inplace": (_I32, [_P, _I32, _I64, _P, _P]),
     "frx_check_range": (_I32, [_P, _I64]),
     "frx_clock_probe": (_I32, [_P, _I32, _P]),
 }

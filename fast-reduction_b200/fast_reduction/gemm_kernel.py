@@ -44,6 +44,16 @@ IGNORE_INDEX = -100
 # Run each chunk's dlogits (HBM-bound) on a side stream so it overlaps the next chunk's forward
 # GEMM (tensor-bound). FRX_OVERLAP_DLOGITS=0 serialises them (for measurement).
 _OVERLAP_DLOGITS = os.environ.get("FRX_OVERLAP_DLOGITS", "1") != "0"
+# The training forward hands its logits to the dlogits pass as fp16 z - m (m = the maximum of the
+# logit's 256-column tile, already in the partials): 2 bytes per logit written and read back
+# instead of 4. FRX_TRAIN_LOGITS=f32 keeps the reference's fp32 logits (for A/B measurement);
+# fp32 operands always use fp32 logits.
+_TILEREL_LOGITS = os.environ.get("FRX_TRAIN_LOGITS", "f16rel") != "f32"
+# The training pass's chunk_size bounds the logits memory, as the reference's per-chunk fp32 logits
+# buffer does (chunk_size x V x 4 bytes): rows go in launches as large as fit that budget, so a
+# vocabulary shard runs fewer forward launches and cross-rank statistics exchanges.
+# FRX_TRAIN_MERGE=0 keeps launches of chunk_size rows (for A/B measurement).
+_TRAIN_MERGE = os.environ.get("FRX_TRAIN_MERGE", "1") != "0"
 _side_streams: dict = {}
 
 
@@ -540,6 +550,20 @@ def gemm_fused_ce_entropy_differentiable(
 gemm_fused_ce_entropy_v2 = gemm_fused_ce_entropy
 
 
+def _train_launch_rows(chunk: int, B: int, ld_logits: int, logit_bytes: int, vocab_size: int) -> int:
+    """Rows per forward launch of the training pass. The budget is the reference's per-chunk fp32
+    logits buffer, chunk x vocab_size x 4 bytes (vocab_size = the whole vocabulary, also on a
+    shard). All rows go in one launch when their logits fit it; otherwise two launch buffers
+    (overlapped dlogits) share it, in multiples of chunk rows, and never fewer than chunk rows."""
+    if not _TRAIN_MERGE:
+        return chunk
+    budget = chunk * max(vocab_size, 1) * 4
+    if B * ld_logits * logit_bytes <= budget:
+        return B
+    rows = budget // (2 * ld_logits * logit_bytes) // chunk * chunk
+    return min(B, max(chunk, rows))
+
+
 def fwd_bwd_shard(
     hidden_2d: Tensor,
     weight: Tensor,
@@ -557,6 +581,7 @@ def fwd_bwd_shard(
     g_ent: Optional[Tensor] = None,
     dhidden_fn=None,
     bias: Optional[Tensor] = None,
+    vocab_size: Optional[int] = None,
 ):
     """Training pass over one vocabulary shard; returns (d_hidden, d_weight [V_shard, H],
     d_bias [V_shard] or None, pending).
@@ -567,28 +592,35 @@ def fwd_bwd_shard(
     is returned instead; ``pairs`` lists the (dlogits, weight) operand pairs whose frx_gemm_dhidden
     products sum to the contribution (one pair, or six bf16x6 pairs for fp32 operands).
 
-    For each row chunk: GEMM epilogue writes the chunk's fp32 logits (and partials); the
-    per-row lse / entropy of the chunk are produced by ``stats_fn(start, end, partials, T, chunk)``
+    Rows go in forward launches of _train_launch_rows rows (chunk_size rows, or more while their
+    logits fit the reference's per-chunk logits budget; ``vocab_size`` is the whole vocabulary,
+    default V_shard). For each launch: the GEMM epilogue writes the launch's logits (fp16 z - m of
+    the logit's tile by default, fp32 for fp32 operands or FRX_TRAIN_LOGITS=f32) and partials; the
+    per-row lse / entropy are produced by ``stats_fn(start, end, partials, T, rows_per_launch)``
     (single GPU: a local finalize; vocabulary-parallel: local merge + cross-rank exchange), which
-    runs on the side stream with the chunk's dlogits when there are several chunks;
-    frx_dlogits writes the chunk's dlogits (in the operands' 16-bit type) into a [B, V_shard] buffer. Then one
-    d_hidden GEMM and one d_weight GEMM over all rows.
+    runs on the side stream with the launch's dlogits when there are several launches; the
+    dlogits kernel writes the launch's dlogits (in the operands' 16-bit type) into a [B, V_shard]
+    buffer. Then one d_hidden GEMM and one d_weight GEMM over all rows.
     """
     B, H = hidden_2d.shape
     V = weight.shape[0]
     dev = hidden_2d.device
-    chunk = _chunk_rows(chunk_size, B)
+    f32 = hidden_2d.dtype == torch.float32
+    rel = _TILEREL_LOGITS and not f32
+    ld_logits = ops.round_up(V, 8 if rel else 4)
+    chunk = _train_launch_rows(_chunk_rows(chunk_size, B), B, ld_logits, 2 if rel else 4,
+                               V if vocab_size is None else vocab_size)
     T = ops.n_vocab_tiles(V)
     n_chunks = (B + chunk - 1) // chunk
     overlap = _OVERLAP_DLOGITS and n_chunks > 1
-    # Two logits (and partials) buffers when the statistics and dlogits of chunk c run on a side
-    # stream under the forward GEMM of chunk c+1 (tensor-bound); the GEMM of chunk c+2 waits for
+    # Two logits (and partials) buffers when the statistics and dlogits of launch c run on a side
+    # stream under the forward GEMM of launch c+1 (tensor-bound); the GEMM of launch c+2 waits for
     # them. The main stream then never waits on a cross-rank statistics exchange.
     n_buf = 2 if overlap else 1
-    logits_bufs = [torch.empty(chunk, ops.round_up(V, 4), device=dev, dtype=torch.float32) for _ in range(n_buf)]
+    logits_bufs = [torch.empty(chunk, ld_logits, device=dev, dtype=torch.float16 if rel else torch.float32)
+                   for _ in range(n_buf)]
     partials_bufs = [torch.empty(T, chunk, 4, device=dev, dtype=torch.float32) for _ in range(n_buf)]
     ldz = ops.round_up(V, 8)
-    f32 = hidden_2d.dtype == torch.float32
     if f32:
         # fp32 operands (the reference's fp32 matmul): the forward GEMM runs on bf16x6 K-concatenated
         # operands (bias folded in), the fp32 dlogits are split into hi / mid / lo parts, and each
@@ -614,20 +646,26 @@ def fwd_bwd_shard(
         if done[buf] is not None:
             main.wait_event(done[buf])
         with ops.phase("frx.train.forward_chunk"):
-            ops.fwd_partials(x_fwd[start:end], w_fwd, target_1d[start:end], partials, chunk, vocab_offset,
-                             logits=logits, bias=fwd_bias)
+            if rel:
+                ops.fwd_partials(x_fwd[start:end], w_fwd, target_1d[start:end], partials, chunk, vocab_offset,
+                                 logits_rel=logits, bias=fwd_bias)
+            else:
+                ops.fwd_partials(x_fwd[start:end], w_fwd, target_1d[start:end], partials, chunk, vocab_offset,
+                                 logits=logits, bias=fwd_bias)
 
         def run_dlogits(logits=logits, partials=partials, start=start, end=end, rows=rows):
             with ops.phase("frx.train.stats"):
                 stats_fn(start, end, partials, T, chunk)
-            ops.dlogits(
-                logits, target_1d[start:end], lse[start:end], entropy[start:end],
-                dz32 if f32 else dz[start:end],
-                rows=rows, vocab_shard=V, ce_weight=ce_weight, ent_weight=ent_weight,
-                g_ce=None if g_ce is None else g_ce[start:end],
-                g_ent=None if g_ent is None else g_ent[start:end],
-                vocab_offset=vocab_offset, ignore_index=ignore_index,
-            )
+            common = dict(rows=rows, vocab_shard=V, ce_weight=ce_weight, ent_weight=ent_weight,
+                          g_ce=None if g_ce is None else g_ce[start:end],
+                          g_ent=None if g_ent is None else g_ent[start:end],
+                          vocab_offset=vocab_offset, ignore_index=ignore_index)
+            if rel:
+                ops.dlogits_tilerel(logits, partials, chunk, target_1d[start:end], lse[start:end],
+                                    entropy[start:end], dz[start:end], **common)
+            else:
+                ops.dlogits(logits, target_1d[start:end], lse[start:end], entropy[start:end],
+                            dz32 if f32 else dz[start:end], **common)
             if f32:
                 ops.split_f32(dz32[:rows, :V], dz_parts[0, start:end], (_HI, _MID, _LO), part_stride=B * ldz)
 
@@ -712,14 +750,41 @@ def _megakernel_fwd_bwd(hidden_2d, weight, target_1d, chunk_size, ce_weight, ent
     return ce, ent, d_hidden, d_weight, d_bias
 
 
-def _scale_grads(dloss: Tensor, *grads):
-    # loss.backward() without an explicit gradient passes exactly 1.0: return the stored
-    # gradients without another full pass over them. Reading dloss on the host synchronises, which
-    # a CUDA-graph capture forbids; while capturing, scale unconditionally (the reference's rule,
-    # gemm_kernel.py:909-915).
-    if dloss.numel() == 1 and not torch.cuda.is_current_stream_capturing() and float(dloss) == 1.0:
-        return grads
-    return tuple(None if g is None else g * dloss for g in grads)
+def _weighted_loss(ce: Tensor, ent: Tensor, ce_weight: float, ent_weight: float) -> Tensor:
+    """0-d fp32 loss = ce_weight * sum(ce) + ent_weight * sum(ent) (reference gemm_kernel.py:897), reduced
+    by one deterministic libfrx kernel."""
+    loss = torch.empty((), device=ce.device, dtype=torch.float32)
+    ops.loss_sum(ce, ent, loss, rows=ce.numel(), ce_weight=ce_weight, ent_weight=ent_weight)
+    return loss
+
+
+def _keep_grads(ctx, *grads) -> None:
+    """Stores the precomputed gradients on the autograd node for _hand_over_grads (not through
+    save_for_backward, whose extra reference would make autograd copy them into .grad)."""
+    ctx.frx_grads = list(grads)
+
+
+def _hand_over_grads(ctx, dloss: Tensor):
+    """The gradients the forward precomputed, scaled by dloss (the reference's `d_hidden * dloss`,
+    gemm_kernel.py:905-913) and handed to autograd.
+
+    The scaling runs in place on the device (frx_scale_inplace, a no-op kernel when dloss is exactly
+    1), so the host never waits for dloss; the node keeps no reference afterwards, so autograd
+    stores the tensors as .grad without copying them. A second backward through the same graph
+    (retain_graph=True) therefore has nothing left to hand over and raises."""
+    grads = getattr(ctx, "frx_grads", None)
+    if grads is None:
+        raise RuntimeError("the gradients of this gemm_megakernel_fast call were already handed to autograd by an "
+                           "earlier backward; a second backward through the same graph is not supported (call the "
+                           "op again instead of using retain_graph=True)")
+    ctx.frx_grads = None
+    scale = dloss.detach().reshape(1)
+    if scale.dtype != torch.float32:
+        scale = scale.to(torch.float32)
+    for g in grads:
+        if g is not None:
+            ops.scale_inplace(g, scale)
+    return grads
 
 
 class GemmMegakernel(torch.autograd.Function):
@@ -732,8 +797,8 @@ class GemmMegakernel(torch.autograd.Function):
         ce, ent, d_hidden, d_weight, d_bias = _megakernel_fwd_bwd(
             hidden_2d, weight_c, target_1d, chunk_size, float(ce_weight), float(ent_weight), IGNORE_INDEX, bias_c,
         )
-        loss = ce_weight * ce.sum() + ent_weight * ent.sum()
-        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight, d_bias)
+        loss = _weighted_loss(ce, ent, float(ce_weight), float(ent_weight))
+        _keep_grads(ctx, d_hidden.view(hidden_states.shape), d_weight, d_bias)
         ce = ce.view(batch_shape)
         ent = ent.view(batch_shape)
         ctx.mark_non_differentiable(ce, ent)
@@ -741,7 +806,7 @@ class GemmMegakernel(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dloss, _g_ce, _g_ent):
-        d_hidden, d_weight, d_bias = _scale_grads(dloss, *ctx.saved_tensors)
+        d_hidden, d_weight, d_bias = _hand_over_grads(ctx, dloss)
         return d_hidden, d_weight, None, d_bias, None, None, None
 
 

@@ -123,9 +123,13 @@ def fwd_partials(
     vocab_offset: int = 0,
     logits: torch.Tensor | None = None,
     bias: torch.Tensor | None = None,
+    logits_rel: torch.Tensor | None = None,
 ) -> None:
-    """partials[t, r] <- (m, s, u, zt) of z = hidden @ weight.T (+ bias) over vocab tile t (see include/frx.h)."""
-    dev = _require_cuda(hidden, weight, target, partials, logits, bias)
+    """partials[t, r] <- (m, s, u, zt) of z = hidden @ weight.T (+ bias) over vocab tile t (see include/frx.h).
+
+    Optionally also writes every logit: fp32 ``logits`` (frx_fwd_partials), or fp16 ``logits_rel`` =
+    z - m of the logit's tile (frx_fwd_partials_tilerel, half the bytes)."""
+    dev = _require_cuda(hidden, weight, target, partials, logits, bias, logits_rel)
     ldh = _row_major(hidden, "hidden")
     ldw = _row_major(weight, "weight")
     rows, hdim = hidden.shape
@@ -148,6 +152,19 @@ def fwd_partials(
         if logits.dtype != torch.float32 or logits.shape[0] < rows or logits.shape[1] < vshard:
             raise ValueError("logits must be float32 [rows, >= vocab_shard]")
     lib = nat.load()
+    if logits_rel is not None:
+        if logits is not None:
+            raise ValueError("pass at most one of logits and logits_rel")
+        ldr = _row_major(logits_rel, "logits_rel")
+        if logits_rel.dtype != torch.float16 or logits_rel.shape[0] < rows or logits_rel.shape[1] < vshard:
+            raise ValueError("logits_rel must be float16 [rows, >= vocab_shard]")
+        rc = _launch("fwd_partials", dev, lambda: lib.frx_fwd_partials_tilerel(
+            hidden.data_ptr(), ldh, weight.data_ptr(), ldw, dt, nat.ptr(bias), nat.ptr(target), rows, vshard, hdim,
+            vocab_offset, partials.data_ptr(), tile_stride, logits_rel.data_ptr(), ldr,
+            nat.status_word(dev).data_ptr(), nat.stream_of(dev),
+        ))
+        nat.check(rc, "frx_fwd_partials_tilerel")
+        return
     rc = _launch("fwd_partials", dev, lambda: lib.frx_fwd_partials(
         hidden.data_ptr(), ldh, weight.data_ptr(), ldw, dt, nat.ptr(bias), nat.ptr(target), rows, vshard, hdim,
         vocab_offset,
@@ -237,6 +254,54 @@ def dlogits(
         nat.stream_of(dev),
     ))
     nat.check(rc, "frx_dlogits")
+
+
+def dlogits_tilerel(
+    logits_rel: torch.Tensor,
+    partials: torch.Tensor,
+    tile_stride: int,
+    target: torch.Tensor | None,
+    lse: torch.Tensor,
+    entropy: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    rows: int,
+    vocab_shard: int,
+    g_ce: torch.Tensor | None = None,
+    g_ent: torch.Tensor | None = None,
+    ce_weight: float = 1.0,
+    ent_weight: float = -1.0,
+    vocab_offset: int = 0,
+    ignore_index: int = NO_IGNORE,
+) -> None:
+    """dlogits (as `dlogits`) from fp16 tile-relative logits z - m_t and the partials holding each tile's
+    maximum m_t (the outputs of one fwd_partials launch with logits_rel)."""
+    dev = _require_cuda(logits_rel, partials, target, lse, entropy, out, g_ce, g_ent)
+    ldl = _row_major(logits_rel, "logits_rel")
+    ldo = _row_major(out, "dlogits")
+    if logits_rel.dtype != torch.float16:
+        raise TypeError("logits_rel must be float16")
+    odt = _OUT_DTYPES.get(out.dtype)
+    if odt is None:
+        raise TypeError("dlogits output must be bfloat16, float16 or float32")
+    if (logits_rel.shape[0] < rows or out.shape[0] < rows or logits_rel.shape[1] < vocab_shard
+            or out.shape[1] < vocab_shard):
+        raise ValueError("logits_rel/out smaller than [rows, vocab_shard]")
+    if partials.dtype != torch.float32 or not partials.is_contiguous() or tile_stride < rows or \
+            partials.numel() < 4 * ((n_vocab_tiles(vocab_shard) - 1) * tile_stride + rows):
+        raise ValueError("partials must be contiguous float32 covering every tile of the launch")
+    for name, t in (("lse", lse), ("entropy", entropy), ("g_ce", g_ce), ("g_ent", g_ent)):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < rows):
+            raise ValueError(f"{name} must be contiguous float32 with >= rows elements")
+    if target is not None and (target.dtype != torch.int64 or not target.is_contiguous() or target.numel() < rows):
+        raise ValueError("target must be a contiguous int64 tensor with one id per row")
+    lib = nat.load()
+    rc = _launch("dlogits", dev, lambda: lib.frx_dlogits_tilerel(
+        logits_rel.data_ptr(), ldl, partials.data_ptr(), tile_stride, nat.ptr(target), lse.data_ptr(),
+        entropy.data_ptr(), nat.ptr(g_ce), nat.ptr(g_ent), float(ce_weight), float(ent_weight), out.data_ptr(), ldo,
+        odt, rows, vocab_shard, vocab_offset, ignore_index, nat.stream_of(dev),
+    ))
+    nat.check(rc, "frx_dlogits_tilerel")
 
 
 def _out_dtype(t: torch.Tensor, accumulate: bool = False) -> int:
@@ -370,3 +435,31 @@ def gemm_dhidden_multicast(dz: torch.Tensor, weight: torch.Tensor, mc_ptr: int, 
         nat.status_word(dev).data_ptr(), nat.stream_of(dev),
     ))
     nat.check(rc, "frx_gemm_dhidden_multicast")
+
+
+def loss_sum(ce: torch.Tensor | None, entropy: torch.Tensor | None, loss: torch.Tensor, *, rows: int,
+             ce_weight: float, ent_weight: float) -> None:
+    """loss (0-d fp32) <- ce_weight * sum(ce[:rows]) + ent_weight * sum(entropy[:rows]) (deterministic)."""
+    dev = _require_cuda(ce, entropy, loss)
+    for name, t in (("ce", ce), ("entropy", entropy)):
+        if t is not None and (t.dtype != torch.float32 or not t.is_contiguous() or t.numel() < rows):
+            raise ValueError(f"{name} must be contiguous float32 with >= rows elements")
+    if loss.dtype != torch.float32 or loss.numel() != 1:
+        raise ValueError("loss must be a one-element float32 tensor")
+    lib = nat.load()
+    rc = _launch("loss_sum", dev, lambda: lib.frx_loss_sum(
+        nat.ptr(ce), nat.ptr(entropy), rows, float(ce_weight), float(ent_weight), loss.data_ptr(), nat.stream_of(dev)))
+    nat.check(rc, "frx_loss_sum")
+
+
+def scale_inplace(x: torch.Tensor, scale: torch.Tensor) -> None:
+    """x *= scale[0] on the device (a no-op kernel when the scale is exactly 1; no host synchronisation)."""
+    dev = _require_cuda(x, scale)
+    if not x.is_contiguous() or x.dtype not in _OUT_DTYPES:
+        raise ValueError("x must be a contiguous bfloat16, float16 or float32 tensor")
+    if scale.dtype != torch.float32 or scale.numel() != 1:
+        raise ValueError("scale must be a one-element float32 tensor")
+    lib = nat.load()
+    rc = _launch("scale_inplace", dev, lambda: lib.frx_scale_inplace(
+        x.data_ptr(), _OUT_DTYPES[x.dtype], x.numel(), scale.data_ptr(), nat.stream_of(dev)))
+    nat.check(rc, "frx_scale_inplace")

@@ -180,7 +180,7 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
     d_hidden_f32, d_weight, d_bias, pending = gk.fwd_bwd_shard(
         hidden_2d, weight_shard, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
         vocab_offset=vocab_start, ignore_index=ignore_index, stats_fn=exchange_stats, dhidden_fn=dhidden_fn,
-        bias=bias_shard,
+        bias=bias_shard, vocab_size=vocab_size,
     )
     if buf is not None:
         hdl.barrier()  # every rank's reductions have landed in every copy
@@ -228,8 +228,8 @@ class VocabParallelMegakernel(torch.autograd.Function):
             hidden_2d, weight_c, target_1d, vocab_start, vocab_size, group, chunk_size, float(ce_weight),
             float(ent_weight), gk.IGNORE_INDEX, bias_c,
         )
-        loss = ce_weight * ce.sum() + ent_weight * ent.sum()
-        ctx.save_for_backward(d_hidden.view(hidden_states.shape), d_weight, d_bias)
+        loss = gk._weighted_loss(ce, ent, float(ce_weight), float(ent_weight))
+        gk._keep_grads(ctx, d_hidden.view(hidden_states.shape), d_weight, d_bias)
         ce = ce.view(batch_shape)
         ent = ent.view(batch_shape)
         ctx.mark_non_differentiable(ce, ent)
@@ -237,7 +237,7 @@ class VocabParallelMegakernel(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dloss, _g_ce, _g_ent):
-        d_hidden, d_weight, d_bias = gk._scale_grads(dloss, *ctx.saved_tensors)
+        d_hidden, d_weight, d_bias = gk._hand_over_grads(ctx, dloss)
         return d_hidden, d_weight, None, None, None, None, None, None, None, d_bias
 
 

@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define FRX_ABI_VERSION 3
+#define FRX_ABI_VERSION 4
 
 #define FRX_OK 0
 #define FRX_ERR_INVALID_ARG 1
@@ -102,6 +102,26 @@ FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* 
                      int64_t ld_logits, int* status, void* stream);
 
 /*
+ * frx_fwd_partials, writing fp16 tile-relative logits instead of fp32 logits: for each row r and
+ * column j of vocabulary tile t,
+ *   logits_rel[r, j] = fp16(z[r, j] - m)     m = the tile maximum this launch writes to slot 0 of
+ *                                             partials[t * tile_stride + r]
+ * rounded to nearest (values below -65504 become -inf). Half the bytes of the fp32 logits; each
+ * stored value is within 2^-11 |z - m| of z - m (2^-25 absolute near 0), so the error of a
+ * probability exp(z - lse) formed from it grows with its distance below its tile's maximum, where
+ * the probabilities themselves shrink as exp(-|z - m|).
+ * frx_dlogits_tilerel reads them back. Replaces, like the fp32 `logits` output of
+ * frx_fwd_partials, the logits store of `_gemm_ce_entropy_bwd_kernel` (fast_reduction/gemm_kernel.py:168-273,
+ * gemm_ce_entropy_bwd_epilogue.py:218), which writes fp32.
+ *   logits_rel  fp16 [rows, ld_logits_rel], 16-byte aligned, ld_logits_rel a multiple of 8
+ */
+FRX_API int frx_fwd_partials_tilerel(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
+                                     int dtype, const void* bias, const int64_t* target, int64_t rows,
+                                     int64_t vocab_shard, int64_t hidden_dim, int64_t vocab_offset, float* partials,
+                                     int64_t tile_stride, void* logits_rel, int64_t ld_logits_rel, int* status,
+                                     void* stream);
+
+/*
  * Merges per-tile partials into per-row results.
  * Replaces the reference's `Finalize` kernel and its custom ops
  * (fast_reduction/gemm_ce_entropy_finalize.py:29-102, 123-212).
@@ -130,6 +150,20 @@ FRX_API int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t* t
                 const float* entropy, const float* g_ce, const float* g_ent, float ce_weight,
                 float ent_weight, void* dlogits, int64_t ld_dlogits, int out_dtype, int64_t rows,
                 int64_t vocab_shard, int64_t vocab_offset, int64_t ignore_index, void* stream);
+
+/*
+ * frx_dlogits from the fp16 tile-relative logits of frx_fwd_partials_tilerel and the partials of the
+ * same launch (tile maximum m_t in slot 0 of partials[t * tile_stride + r]):
+ *   log p = max(logits_rel, -65504) - (lse - m_t),  dz = p * (g_ce - g_ent * (log p + H)) - g_ce * [j == target]
+ * Reads 2 bytes per logit instead of 4. Same arguments and rules as frx_dlogits otherwise.
+ * Replaces `ComputeDlogits` / `compute_dlogits` (fast_reduction/cute_dlogits.py:32-100, 162-183)
+ * in the training pass.
+ */
+FRX_API int frx_dlogits_tilerel(const void* logits_rel, int64_t ld_logits_rel, const float* partials,
+                                int64_t tile_stride, const int64_t* target, const float* lse, const float* entropy,
+                                const float* g_ce, const float* g_ent, float ce_weight, float ent_weight,
+                                void* dlogits, int64_t ld_dlogits, int out_dtype, int64_t rows, int64_t vocab_shard,
+                                int64_t vocab_offset, int64_t ignore_index, void* stream);
 
 /*
  * d_hidden[rows, hidden_dim] = dlogits[rows, vocab_shard] @ weight[vocab_shard, hidden_dim]
@@ -224,6 +258,25 @@ FRX_API int frx_fwd_ce_entropy_noalloc(const void* hidden, int64_t ld_hidden, co
                                        int64_t vocab_size, int64_t hidden_dim, int64_t ignore_index,
                                        float* ce, float* entropy, float* lse, float* log_probs, int* status,
                                        void* stream);
+
+/*
+ * loss[0] = ce_weight * sum_r ce[r] + ent_weight * sum_r entropy[r] over `rows` fp32 values (either
+ * input may be NULL and then counts as zero), accumulated in fp64 in a fixed order: deterministic.
+ * Replaces the reference's `ce_weight * ce.sum() + ent_weight * ent.sum()`
+ * (fast_reduction/gemm_kernel.py:897).
+ */
+FRX_API int frx_loss_sum(const float* ce, const float* entropy, int64_t rows, float ce_weight, float ent_weight,
+                         float* loss, void* stream);
+
+/*
+ * x[i] *= scale[0] for n elements of dtype FRX_DTYPE_BF16, _F16 or _F32 (16-bit values are scaled in
+ * fp32 and rounded to nearest). The scale is read on the device when the kernel runs; when it is
+ * exactly 1 the kernel returns without touching x, so the caller needs no host synchronisation to
+ * skip the work. Replaces the reference's `d_hidden * dloss` / `d_weight * dloss` in the
+ * megakernel's backward (fast_reduction/gemm_kernel.py:905-913), done in place on the stored
+ * gradients.
+ */
+FRX_API int frx_scale_inplace(void* x, int dtype, int64_t n, const float* scale, void* stream);
 
 /*
  * FRX_OK when the `bytes` bytes from `ptr` lie inside one device allocation (cuMemGetAddressRange),

@@ -263,6 +263,33 @@ def dlogits(logits: np.ndarray, target: np.ndarray, lse: np.ndarray, ent: np.nda
     return dz
 
 
+def tile_relative_logits(logits32: torch.Tensor, tile: int = VOCAB_TILE) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(fp16 d = z - m_t, fp32 m [T, M]) of fp32 logits [M, V]: m_t is the maximum of the row over
+    the logit's `tile`-column tile, d the fp32 difference rounded to nearest fp16.
+
+    Not a reference format: the reference stores the fp32 logits themselves
+    (gemm_ce_entropy_bwd_epilogue.py:218) for its dlogits kernel (cute_dlogits.py:87-100). This
+    restates the engine's 2-byte hand-over of the same logits so the tests can check it bit for
+    bit; dlogits() of (d + m_t) then gives the gradient the engine forms from it, since
+    log p = d - (lse - m_t) = (d + m_t) - lse.
+    """
+    z = logits32.float()
+    M, V = z.shape
+    T = (V + tile - 1) // tile
+    m = torch.empty(T, M, dtype=torch.float32, device=z.device)
+    d = torch.empty(M, V, dtype=torch.float16, device=z.device)
+    for t in range(T):
+        blk = z[:, t * tile:min((t + 1) * tile, V)]
+        m[t] = blk.max(dim=1).values
+        d[:, t * tile:min((t + 1) * tile, V)] = (blk - m[t][:, None]).to(torch.float16)
+    return d, m
+
+
+def expand_tile_max(m: torch.Tensor, V: int, tile: int = VOCAB_TILE) -> torch.Tensor:
+    """[T, M] per-tile maxima -> [M, V] (each column gets its tile's maximum)."""
+    return m.t().repeat_interleave(tile, dim=1)[:, :V]
+
+
 # ---------------------------------------------------------------------------------------------
 # Seeded inputs with the BASELINE.json distributions
 # ---------------------------------------------------------------------------------------------

@@ -104,6 +104,29 @@ def test_forward_launch_rows():
     assert gk._launch_rows(4096, 65536, T(1 << 24)) == 4096     # partials of one chunk exceed the budget
 
 
+def test_training_launch_rows():
+    """chunk_size caps the training pass's logits memory at the reference's per-chunk fp32 logits
+    buffer (chunk x V x 4 bytes): all rows in one launch when they fit, else two buffers of a
+    multiple of chunk rows, never fewer than chunk rows."""
+    V = 128256
+    ld16, ld32 = ops.round_up(V, 8), ops.round_up(V, 4)
+    # one GPU, headline: 2-byte logits give two 4096-row buffers (= one fp32 chunk buffer)
+    assert gk._train_launch_rows(4096, 32768, ld16, 2, V) == 4096
+    assert gk._train_launch_rows(4096, 32768, ld32, 4, V) == 4096
+    # vocabulary shards of the headline over 2 / 4 / 8 GPUs
+    assert gk._train_launch_rows(4096, 32768, ops.round_up(64128, 8), 2, V) == 8192
+    assert gk._train_launch_rows(4096, 32768, ops.round_up(32064, 8), 2, V) == 32768
+    assert gk._train_launch_rows(4096, 32768, ops.round_up(16032, 8), 2, V) == 32768
+    # fewer rows than a chunk, and the opt-out
+    assert gk._train_launch_rows(4096, 100, ld16, 2, V) == 100
+    old = gk._TRAIN_MERGE
+    try:
+        gk._TRAIN_MERGE = False
+        assert gk._train_launch_rows(4096, 32768, ops.round_up(16032, 8), 2, V) == 4096
+    finally:
+        gk._TRAIN_MERGE = old
+
+
 def test_host_upload_plan():
     """Upload schedule of the host-streamed forward (no GPU needed): a weight head before the hidden
     when both are on the host, hidden chunks only with a head, and weight slices that start small,
