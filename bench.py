@@ -5,7 +5,9 @@ Workload: B=32768, H=4096, V=128256, bf16, chunk 4096
 weight ~ N(0, 0.02), targets uniform. One step = one forward over the whole batch through the
 public API (`gemm_fused_ce_entropy`; vocabulary-parallel `vocab_parallel_ce_entropy` for N > 1).
 The same line also reports the training step (`gemm_megakernel_fast` + loss.backward(), configs[2])
-under "fwd_bwd".
+under "fwd_bwd", BASELINE.json configs[3] and configs[4] under "configs" (few steps each), and at every
+N the accuracy of the sharded result against an fp32 ground truth merged over the shards (forward CE /
+entropy over all rows, d_hidden rows, d_weight rows of every shard).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     python bench.py --micro        (HBM-bound kernels alone: finalize, dlogits, column sums, fp32 split,
@@ -243,22 +245,150 @@ def time_steps(step, steps: int, warmup: int, world: int, timer: KernelTimer | N
 
 
 # ------------------------------------------------------------------------------------------------ inputs
-def make_headline_inputs(B, H, V, vstart, vend, seed=0):
+def make_headline_inputs(B, H, V, vstart, vend, seed=0, weight_std=0.02):
+    """hidden ~ N(0, 1) [B, H], this rank's rows [vstart, vend) of a weight ~ N(0, weight_std) [V, H],
+    targets uniform in [0, V): bf16, drawn on the device. The weight is drawn in 8192-row blocks with
+    per-block seeds, so every rank sees the same slice values for any number of ranks."""
     g = torch.Generator(device="cuda").manual_seed(seed)
     hidden = torch.randn(B, H, device="cuda", generator=g).to(torch.bfloat16)
     weight = torch.empty(vend - vstart, H, device="cuda", dtype=torch.bfloat16)
-    # the full weight is drawn in row blocks so every rank sees the same slice values for any N
     blk = 8192
     for r0 in range(0, V, blk):
         r1 = min(r0 + blk, V)
-        gb = torch.Generator(device="cuda").manual_seed(seed * 1_000_003 + r0 + 1)
         lo, hi = max(r0, vstart), min(r1, vend)
         if lo >= hi:
             continue
-        rows = (torch.randn(r1 - r0, H, device="cuda", generator=gb) * 0.02).to(torch.bfloat16)
+        gb = torch.Generator(device="cuda").manual_seed(seed * 1_000_003 + r0 + 1)
+        rows = (torch.randn(r1 - r0, H, device="cuda", generator=gb) * weight_std).to(torch.bfloat16)
         weight[lo - vstart:hi - vstart] = rows[lo - r0:hi - r0]
     target = torch.randint(0, V, (B,), device="cuda", generator=g)
     return hidden, weight, target
+
+
+def make_config_inputs(cfg: dict, world: int, rank: int):
+    """BASELINE.json configs[3] / configs[4] inputs for this rank (seeded, identical on every rank):
+    configs[3] sets a seeded 5% of the targets to ignore_index -100; configs[4] moves a seeded 1% of
+    the targets into the last 256-column tile of a vocabulary shard (the ragged one when the shard
+    width is not a multiple of 256), spread over the shards of this run."""
+    from fast_reduction import vocab_parallel as vp
+
+    B, H, V = cfg["B"], cfg["H"], cfg["V"]
+    vstart, vend = vp.shard_bounds(V, world, rank)
+    hidden, weight, target = make_headline_inputs(B, H, V, vstart, vend, seed=cfg["seed"], weight_std=cfg["wstd"])
+    g = torch.Generator().manual_seed(cfg["seed"] + 7)
+    t = target.cpu()
+    if cfg.get("tail_frac"):
+        n = int(round(cfg["tail_frac"] * B))
+        idx = torch.randperm(B, generator=g)[:n]
+        for j, i in enumerate(idx.tolist()):
+            a, b = vp.shard_bounds(V, world, j % world)
+            last = a + (b - a - 1) // 256 * 256
+            t[i] = int(torch.randint(last, b, (1,), generator=g))
+    if cfg.get("ignore_frac"):
+        n = int(round(cfg["ignore_frac"] * B))
+        t[torch.randperm(B, generator=g)[:n]] = -100
+    return hidden, weight, t.to(hidden.device), vstart, vend
+
+
+# ------------------------------------------------------------------------------------------------ accuracy
+def fp32_stats(hidden, weight_shard, target, vstart, world, rows=None, chunk=2048):
+    """fp32 ground truth per row over the whole vocabulary (fp32 logits, TF32 off, fp64 reductions):
+    each rank reduces its shard's fp32 logits to (m, s, u, zt), the ranks all-gather them and merge.
+    Returns fp64 (lse, entropy, ce-before-ignore) for the first `rows` rows (default all)."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    B = hidden.shape[0] if rows is None else rows
+    V_r = weight_shard.shape[0]
+    wf = weight_shard.float()
+    st = torch.empty(B, 4, device=hidden.device, dtype=torch.float64)
+    for r0 in range(0, B, chunk):
+        r1 = min(B, r0 + chunk)
+        z = (hidden[r0:r1].float() @ wf.T).double()
+        m = z.max(dim=1).values
+        d = z - m[:, None]
+        e = d.exp()
+        st[r0:r1, 0] = m
+        st[r0:r1, 1] = e.sum(1)
+        st[r0:r1, 2] = (d * e).sum(1)
+        lt = target[r0:r1] - vstart
+        inside = (lt >= 0) & (lt < V_r)
+        zt = torch.zeros(r1 - r0, device=z.device, dtype=torch.float64)
+        zt[inside] = z[inside.nonzero().squeeze(1), lt[inside]]
+        st[r0:r1, 3] = zt
+        del z, d, e
+    if world > 1:
+        allst = torch.empty(world * B, 4, device=st.device, dtype=st.dtype)
+        dist.all_gather_into_tensor(allst, st)
+        allst = allst.view(world, B, 4)
+    else:
+        allst = st.view(1, B, 4)
+    M = allst[:, :, 0].max(dim=0).values
+    dm = allst[:, :, 0] - M[None]
+    sc = dm.exp()
+    S = (allst[:, :, 1] * sc).sum(0)
+    U = ((allst[:, :, 2] + dm * allst[:, :, 1]) * sc).sum(0)
+    ZT = allst[:, :, 3].sum(0)
+    lse = M + S.log()
+    ent = S.log() - U / S
+    return lse, ent, lse - ZT
+
+
+def _dz_fp32(z, target_rows, cols_global, lse, ent, ce_weight=1.0, ent_weight=-1.0):
+    """dlogits of loss = ce_weight sum ce + ent_weight sum H for fp32 logits z [R, C] whose columns
+    are the global vocabulary ids `cols_global`, given fp64 per-row lse / entropy (ignore_index
+    -100 rows drop the CE term)."""
+    lp = z.double() - lse[:, None]
+    p = lp.exp()
+    gce = torch.where(target_rows == -100, 0.0, ce_weight).double()
+    dz = p * (gce - ent_weight * ent)[:, None] - ent_weight * p * lp
+    hit = target_rows[:, None] == cols_global[None, :]
+    dz = dz - hit.double() * gce[:, None]
+    return dz
+
+
+def sharded_accuracy(ce, ent, hidden, weight_shard, target, vstart, world, grads=None, rows_check=None,
+                     dh_rows=256, dw_rows=256):
+    """Forward (and, with grads = (d_hidden, d_weight_shard), training) accuracy of the engine against
+    the fp32 ground truth at any number of ranks, with the north-star gates (CE MAE <= 2e-3, entropy
+    MAE <= 1e-4, dH / dW MAE <= 2e-3). d_hidden is checked on its first dh_rows rows (each rank's fp32
+    contribution from its shard, summed over ranks); d_weight on dw_rows vocabulary rows spread over
+    each rank's own shard (incl. its last, possibly ragged, tile), against every row of the batch;
+    the reported dW MAE is the maximum over ranks."""
+    lse, ent32, ce_raw = fp32_stats(hidden, weight_shard, target, vstart, world, rows=rows_check)
+    n = lse.shape[0]
+    ign = target[:n] == -100
+    ce32 = torch.where(ign, 0.0, ce_raw)
+    out = {"rows_checked": n,
+           "ce_mae": float((ce.reshape(-1)[:n].double() - ce32).abs().mean()),
+           "ent_mae": float((ent.reshape(-1)[:n].double() - ent32).abs().mean()),
+           "reference": "fp32 logits (TF32 off), fp64 reductions, merged over shards"}
+    if grads is None:
+        return out, (lse, ent32)
+    d_hidden, d_weight = grads
+    V_r = weight_shard.shape[0]
+    wf = weight_shard.float()
+    # d_hidden rows [0, dh_rows): this shard's fp32 contribution, summed over ranks
+    R = min(dh_rows, n)
+    z = hidden[:R].float() @ wf.T
+    cols = torch.arange(vstart, vstart + V_r, device=z.device)
+    dz = _dz_fp32(z, target[:R], cols, lse[:R], ent32[:R])
+    dh = (dz.float() @ wf)
+    if world > 1:
+        dist.all_reduce(dh)
+    out["dh_mae"] = float((d_hidden.reshape(-1, hidden.shape[1])[:R].float() - dh).abs().mean())
+    out["dh_rows_checked"] = R
+    # d_weight rows of this shard, against every row (needs the fp32 statistics of all rows)
+    if n == hidden.shape[0]:
+        sel = torch.unique(torch.cat([torch.linspace(0, V_r - 1, dw_rows - 8, device=z.device).round().long(),
+                                      torch.arange(max(0, V_r - 8), V_r, device=z.device)]))
+        zs = hidden.float() @ wf[sel].T
+        dzs = _dz_fp32(zs, target, vstart + sel, lse, ent32)
+        dws = dzs.float().T @ hidden.float()
+        mae = torch.tensor([float((d_weight[sel].float() - dws).abs().mean())], device=z.device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(mae, op=dist.ReduceOp.MAX)
+        out["dw_mae"] = float(mae)
+        out["dw_rows_checked_per_rank"] = int(sel.numel())
+    return out, (lse, ent32)
 
 
 # ------------------------------------------------------------------------------------------------ cpu baseline
@@ -324,9 +454,18 @@ def _cpu_model() -> str:
     return "unknown"
 
 
+# Bound on the whole --impl reference run (warm-up + timed steps) on the host cores.
+_REFERENCE_BUDGET_S = 240.0
+
+
 def run_reference(args, world, rank):
-    """--impl reference: the reference's own algorithm for this path on the host cores (the oracle
-    port of baseline.chunked_linear_xent_entropy; the reference's Python cannot travel to the box)."""
+    """--impl reference: the reference's own algorithm for this path on the host cores: the oracle
+    restatement of baseline.chunked_linear_xent_entropy (baseline.py:207-241), bit-exact against the
+    reference's golden outputs (tests/test_oracle.py). The reference package itself cannot be
+    installed here (its build backend, hatchling, is not in the offline wheelhouse), and its Python
+    cannot travel to the GPU box. Each step runs the whole batch of B rows when warm-up + timed
+    steps fit _REFERENCE_BUDGET_S (no extrapolation), else an equal row sample per step, scaled to B.
+    Under torchrun only rank 0 runs; the other ranks exit without work."""
     if rank != 0:
         return
     from oracle import reference_math as rm
@@ -336,25 +475,34 @@ def run_reference(args, world, rank):
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(0)
     weight = (torch.randn(V, H, generator=g) * 0.02).to(torch.bfloat16)
-    # size one step (a row sample) for ~3 s of CPU work so warmup + steps finish in minutes
-    h = torch.randn(64, H, generator=g).to(torch.bfloat16)
-    t = torch.randint(0, V, (64,), generator=g)
+    hidden = torch.randn(B, H, generator=g).to(torch.bfloat16)
+    target = torch.randint(0, V, (B,), generator=g)
+    # probe one chunk to size the step
     t0 = time.perf_counter()
-    rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
-    probe = time.perf_counter() - t0
-    rows = int(max(64, min(4096, 64 * 3.0 / max(probe, 1e-3)))) // 64 * 64
-    h = torch.randn(rows, H, generator=g).to(torch.bfloat16)
-    t = torch.randint(0, V, (rows,), generator=g)
+    rm.chunked_linear_xent_entropy(hidden[:chunk], weight, target[:chunk], chunk_size=chunk)
+    per_row = (time.perf_counter() - t0) / min(chunk, B)
+    n_steps = max(1, args.steps + args.warmup)
+    rows = B
+    if per_row * B * n_steps > _REFERENCE_BUDGET_S:
+        rows = max(chunk, int(_REFERENCE_BUDGET_S / n_steps / per_row) // chunk * chunk)
+    h, t = hidden[:rows], target[:rows]
     for _ in range(args.warmup):
         rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
     times = []
+    t_all = time.perf_counter()
     for _ in range(args.steps):
         t0 = time.perf_counter()
         rm.chunked_linear_xent_entropy(h, weight, t, chunk_size=chunk)
         times.append(time.perf_counter() - t0)
-    per_step = statistics.median(times)
+    timed_s = time.perf_counter() - t_all
+    per_step = sum(times) / len(times)
     ms_full = per_step * 1000.0 * B / rows
     flops = 2.0 * B * H * V
+    full = rows == B
+    sample = (f"each step: all {B} rows (full V={V}, H={H}), mean of {args.steps} steps; timed region {timed_s:.1f} s"
+              if full else
+              f"each step: {rows} of {B} rows (full V, H), mean of {args.steps} steps = {per_step:.2f} s, scaled "
+              f"linearly to B={B} (the whole batch x {n_steps} steps would exceed {_REFERENCE_BUDGET_S:.0f} s)")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(ms_full, 1), "unit": "ms", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_full, 1), "higher_is_better": False,
@@ -363,14 +511,106 @@ def run_reference(args, world, rank):
                    "l2": "inputs larger than L2"},
         "tflops": round(flops / (ms_full / 1000.0) / 1e12, 3),
         "cpu_baseline": {"value": round(ms_full, 1), "unit": "ms", "cores": threads, "kind": "port",
-                         "sample": f"each step: {rows} of {B} rows (full V, H), median of {args.steps} steps "
-                                   f"= {per_step:.2f} s, extrapolated linearly to B={B}"},
+                         "sample": sample, "extrapolated": not full, "cpu_model": _cpu_model(),
+                         "implementation": "oracle/reference_math.chunked_linear_xent_entropy (restates reference "
+                                           "baseline.py:207-241; reference install unavailable: no hatchling)"},
         "e2e": {"value": round(ms_full, 1), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 # ------------------------------------------------------------------------------------------------ our engine
+# BASELINE.json configs[3] (large-vocabulary entropy stress) and configs[4] (ragged tail), timed with
+# few steps at every N beside the headline, each with its own accuracy check.
+CONFIGS = {
+    "configs[3]": {"workload": "configs[3] large-vocab stress: hidden [8, 2048, 4096], V=256000, weight N(0, 0.05), "
+                               "5% targets ignore_index", "B": 16384, "H": 4096, "V": 256000, "chunk": 4096,
+                   "wstd": 0.05, "ignore_frac": 0.05, "seed": 3, "hidden_shape": (8, 2048)},
+    "configs[4]": {"workload": "configs[4] ragged tail: B=65536, H=5120, V=152064, chunk 8192, 1% targets in a "
+                               "shard's last vocabulary tile", "B": 65536, "H": 5120, "V": 152064, "chunk": 8192,
+                   "wstd": 0.02, "tail_frac": 0.01, "seed": 4},
+}
+# The N=1 run leaves its clock-normalised fractions here, so later N>1 runs of the same workload on
+# the same box can report their efficiency at equal clocks.
+_N1_STATE = Path("/tmp/frx_bench_n1.json")
+
+
+def _train_fn(gk, vp, world, h_leaf, w_leaf, target, vstart, V, chunk):
+    def train_step():
+        h_leaf.grad = None
+        w_leaf.grad = None
+        if world == 1:
+            loss, _, _ = gk.gemm_megakernel_fast(h_leaf, w_leaf, target, chunk_size=chunk)
+        else:
+            loss, _, _ = vp.vocab_parallel_megakernel(h_leaf, w_leaf, target, vstart, V, chunk_size=chunk)
+        loss.backward()
+    return train_step
+
+
+def _fwd_fn(gk, vp, world, hidden, weight, target, vstart, V, chunk):
+    if world == 1:
+        return lambda: gk.gemm_fused_ce_entropy(hidden, weight, target, chunk_size=chunk)
+    return lambda: vp.vocab_parallel_ce_entropy(hidden, weight, target, vstart, V, chunk_size=chunk)
+
+
+def _gpu_numa_node(index: int):
+    """NUMA node of GPU `index` from its PCI address (None when the system does not say)."""
+    try:
+        pr = torch.cuda.get_device_properties(index)
+        addr = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        node = int(Path(f"/sys/bus/pci/devices/{addr}/numa_node").read_text().strip())
+        return node if node >= 0 else None
+    except Exception:
+        return None
+
+
+def _node_cpus(node: int):
+    try:
+        out = set()
+        for part in Path(f"/sys/devices/system/node/node{node}/cpulist").read_text().strip().split(","):
+            a, _, b = part.partition("-")
+            out.update(range(int(a), int(b or a) + 1))
+        return out
+    except Exception:
+        return None
+
+
+def run_config(name, cfg, world, rank, local, steps, warmup, peaks):
+    """Forward and training step of one BASELINE config at this N (few steps), with accuracy."""
+    from fast_reduction import gemm_kernel as gk
+    from fast_reduction import vocab_parallel as vp
+
+    B, H, V, chunk = cfg["B"], cfg["H"], cfg["V"], cfg["chunk"]
+    hidden, weight, target, vstart, vend = make_config_inputs(cfg, world, rank)
+    shape = cfg.get("hidden_shape")
+    hs = hidden.view(*shape, H) if shape else hidden
+    ts = target.view(*shape) if shape else target
+    fwd = _fwd_fn(gk, vp, world, hs, weight, ts, vstart, V, chunk)
+    fwd_ms, fclk = time_steps(fwd, steps, warmup, world, sampler=ClockSampler(local))
+    h_leaf = hs.detach().requires_grad_(True)
+    w_leaf = weight.detach().requires_grad_(True)
+    train = _train_fn(gk, vp, world, h_leaf, w_leaf, ts, vstart, V, chunk)
+    fb_ms, bclk = time_steps(train, steps, warmup, world, sampler=ClockSampler(local))
+    train()
+    ce, ent, _ = fwd()
+    acc, _ = sharded_accuracy(ce, ent, hidden, weight, target, vstart, world, grads=(h_leaf.grad, w_leaf.grad),
+                              rows_check=1024, dh_rows=128)
+    peak_tf = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    ff, fbf = 2.0 * B * H * V, 6.0 * B * H * V
+    res = {"workload": cfg["workload"], "B": B, "H": H, "V": V, "chunk": chunk, "steps": steps, "warmup": warmup,
+           "fwd_ms": round(fwd_ms, 3), "fwd_bwd_ms": round(fb_ms, 3),
+           "fwd_frac_of_peak": round(ff / (fwd_ms / 1e3) / 1e12 / (peak_tf * world), 4),
+           "fwd_bwd_frac_of_peak": round(fbf / (fb_ms / 1e3) / 1e12 / (peak_tf * world), 4),
+           "fwd_frac_of_clock_limited_peak": _clock_frac(ff / (fwd_ms / 1e3) / 1e12 / world, fclk),
+           "fwd_bwd_frac_of_clock_limited_peak": _clock_frac(fbf / (fb_ms / 1e3) / 1e12 / world, bclk),
+           "sm_mhz_effective": {"fwd": (fclk or {}).get("sm_mhz_effective"),
+                                "fwd_bwd": (bclk or {}).get("sm_mhz_effective")},
+           "accuracy": acc}
+    del hidden, weight, target, hs, ts, h_leaf, w_leaf, ce, ent
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args, world, rank, local):
     from fast_reduction import _native as nat
     from fast_reduction import gemm_kernel as gk
@@ -383,13 +623,7 @@ def run_ours(args, world, rank, local):
     peaks = load_peaks()
     hidden, weight, target = make_headline_inputs(B, H, V, vstart, vend, seed=0)
     torch.cuda.synchronize()
-
-    if world == 1:
-        def fwd():
-            return gk.gemm_fused_ce_entropy(hidden, weight, target, chunk_size=chunk)
-    else:
-        def fwd():
-            return vp.vocab_parallel_ce_entropy(hidden, weight, target, vstart, V, chunk_size=chunk)
+    fwd = _fwd_fn(gk, vp, world, hidden, weight, target, vstart, V, chunk)
 
     # ---- forward (headline value) with per-kernel event timing and clock sampling
     timer = KernelTimer()
@@ -412,21 +646,7 @@ def run_ours(args, world, rank, local):
     achieved_tflops = gemm_flops / (gemm_avg_ms / 1000.0) / 1e12
     peak_tf = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     peak_sus = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
-
-    # accuracy spot check on 512 rows against fp32 torch (TF32 off)
     ce, ent, lp = fwd()
-    torch.backends.cuda.matmul.allow_tf32 = False
-    acc = {}
-    if world == 1:
-        n = 512
-        z = hidden[:n].float() @ weight.float().T
-        lse = torch.logsumexp(z, -1)
-        ls = z - lse[:, None]
-        ce32 = lse - z[torch.arange(n, device=z.device), target[:n]]
-        ent32 = -(ls.exp() * ls).sum(-1)
-        acc = {"ce_mae": float((ce[:n] - ce32).abs().mean()), "ent_mae": float((ent[:n] - ent32).abs().mean()),
-               "rows_checked": n}
-        del z, ls
 
     # ---- configs[0] (B=1024, H=1024, V=32000, chunk 512): a launch-bound size, eager vs CUDA graph
     small = None
@@ -448,23 +668,11 @@ def run_ours(args, world, rank, local):
 
     # ---- fwd+bwd (training step, configs[2])
     fb = None
+    grads = None
     if not args.no_fwd_bwd:
         h_leaf = hidden.detach().requires_grad_(True)
         w_leaf = weight.detach().requires_grad_(True)
-
-        if world == 1:
-            def train_step():
-                h_leaf.grad = None
-                w_leaf.grad = None
-                loss, _, _ = gk.gemm_megakernel_fast(h_leaf, w_leaf, target, chunk_size=chunk)
-                loss.backward()
-        else:
-            def train_step():
-                h_leaf.grad = None
-                w_leaf.grad = None
-                loss, _, _ = vp.vocab_parallel_megakernel(h_leaf, w_leaf, target, vstart, V, chunk_size=chunk)
-                loss.backward()
-
+        train_step = _train_fn(gk, vp, world, h_leaf, w_leaf, target, vstart, V, chunk)
         timer_fb = KernelTimer()
         fb_steps = max(1, min(args.steps, 10))
         torch.cuda.reset_peak_memory_stats(dev)
@@ -472,6 +680,14 @@ def run_ours(args, world, rank, local):
         fb_ms, fb_clocks = time_steps(train_step, fb_steps, max(args.warmup, 1), world, timer_fb, ClockSampler(local))
         peak_extra_fb = (torch.cuda.max_memory_allocated(dev) - mem_base_fb) / 1e9
         kfb = timer_fb.summary()
+        # The same step with the dlogits pass serialised on the main stream: per-kernel times without
+        # the side stream's waits for SMs (the overlapped figures above include them).
+        prev_overlap = gk._OVERLAP_DLOGITS
+        gk._OVERLAP_DLOGITS = False
+        timer_ser = KernelTimer()
+        ser_ms, _ = time_steps(train_step, 2, 1, world, timer_ser)
+        gk._OVERLAP_DLOGITS = prev_overlap
+        kser = timer_ser.summary()
         flops_fb = 6.0 * B * H * V
         fb = {"ms": round(fb_ms, 3), "tflops": round(flops_fb / (fb_ms / 1000.0) / 1e12, 1),
               "frac_of_peak": round(flops_fb / (fb_ms / 1000.0) / 1e12 / (peak_tf * world), 4),
@@ -480,49 +696,42 @@ def run_ours(args, world, rank, local):
               "steps": fb_steps,
               "workload": "configs[2] gemm_megakernel_fast + loss.backward(), ce_weight 1, ent_weight -1",
               "peak_extra_mem_gb": round(peak_extra_fb, 3),
-              "kernels_ms_per_step": {k: round(v["total_ms"] / fb_steps, 3) for k, v in kfb.items()},
+              "kernels_ms_per_step_wall": {k: round(v["total_ms"] / fb_steps, 3) for k, v in kfb.items()},
+              "kernels_ms_per_step_wall_note": "events around each launch on its own stream while the dlogits pass "
+                                               "overlaps the next forward GEMM: includes time spent waiting for SMs",
+              "kernels_ms_per_step": {k: round(v["total_ms"] / 2, 3) for k, v in kser.items()},
+              "kernels_ms_per_step_note": f"serialised pass (FRX_OVERLAP_DLOGITS=0, 2 steps, {ser_ms:.2f} ms/step): "
+                                          "each kernel alone on the stream",
               "gpu_launches_per_step": timer_fb.count // fb_steps, "clocks": fb_clocks}
-        if world == 1:
-            n = 256
-            hs = hidden[:n].detach().float().requires_grad_(True)
-            z = hs @ weight.float().T
-            ls = torch.log_softmax(z, -1)
-            l = torch.nn.functional.nll_loss(ls, target[:n], reduction="sum") + (ls.exp() * ls).sum()
-            l.backward()
-            train_step()
-            fb["dh_mae_rows_checked"] = n
-            fb["dh_mae"] = float((h_leaf.grad[:n].float() - hs.grad).abs().mean())
-            fb["dh_rel_err"] = float((h_leaf.grad[:n].float() - hs.grad).norm() / hs.grad.norm())
-            del z, ls, hs
+        train_step()
+        grads = (h_leaf.grad, w_leaf.grad)
+
+    # ---- accuracy at every N: fp32 ground truth over the shards, forward over all rows, gradients
+    acc, _ = sharded_accuracy(ce, ent, hidden, weight, target, vstart, world, grads=grads)
+    if fb is not None:
+        fb["accuracy"] = {k: acc[k] for k in ("dh_mae", "dh_rows_checked", "dw_mae", "dw_rows_checked_per_rank")
+                          if k in acc}
+        fb["accuracy"]["gate"] = "dH / dW MAE <= 2e-3 vs fp32"
         h_leaf.grad = None
         w_leaf.grad = None
-        del h_leaf, w_leaf
+        del h_leaf, w_leaf, grads
+    acc = {k: acc[k] for k in ("rows_checked", "ce_mae", "ent_mae", "reference")}
+    acc["gate"] = "CE MAE <= 2e-3, entropy MAE <= 1e-4 vs fp32"
+    del ce, ent, lp
+    torch.cuda.empty_cache()
 
     # ---- end to end through the public API with host buffers (H2D inputs, D2H results inside)
     e2e = None
     if not args.no_e2e:
-        h_host = hidden.cpu().pin_memory()
-        w_host = weight.cpu().pin_memory()
-        t_host = target.cpu().pin_memory()
+        e2e = run_e2e(gk, vp, world, rank, local, hidden, weight, target, vstart, V, chunk, args)
 
-        # The public API takes the host tensors itself: it uploads them (the weight in slices
-        # under the GEMMs; with N ranks each uploads 1/N of the hidden rows and all-gathers them)
-        # and returns host results, waiting for them.
-        def e2e_step():
-            if world == 1:
-                res = gk.gemm_fused_ce_entropy(h_host, w_host, t_host, chunk_size=chunk)
-            else:
-                res = vp.vocab_parallel_ce_entropy(h_host, w_host, t_host, vstart, V, chunk_size=chunk)
-            assert res[0].device.type == "cpu"
-
-        e2e_ms, _ = time_steps(e2e_step, max(1, min(args.steps, 10)), max(args.warmup, 3), world)
-        hidden_share = (B + world - 1) // world
-        h2d = hidden_share * H * 2 + w_host.numel() * 2 + t_host.numel() * 8
-        e2e = {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(3 * B * 4),
-               "path": "pinned host hidden/weight(shard)/target -> gemm_fused_ce_entropy (host in, host out; "
-                       "bytes per rank)"}
-        del h_host, w_host, t_host
+    # ---- BASELINE configs[3] / configs[4] at this N
+    cfgs = None
+    if not args.no_configs:
+        del hidden, weight, target
+        torch.cuda.empty_cache()
+        cfgs = {name: run_config(name, cfg, world, rank, local, args.config_steps, 3, peaks)
+                for name, cfg in CONFIGS.items()}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -545,6 +754,9 @@ def run_ours(args, world, rank, local):
     headline_shape = (B, H, V, chunk) == (32768, 4096, 128256, 4096)
     if fb is not None and headline_shape:
         fb["vs_baseline"] = round(fb["ms"] / REFERENCE_PUBLISHED_MS["fwd_bwd"], 4)
+    fwd_clock_frac = _clock_frac(tflops / world, clocks)
+    scaling_cn = _clock_normalised_scaling(world, (B, H, V, chunk), fwd_clock_frac,
+                                           None if fb is None else fb["frac_of_clock_limited_peak"])
     line = {
         "metric": METRIC,
         "value": round(fwd_ms, 3),
@@ -566,11 +778,12 @@ def run_ours(args, world, rank, local):
         "tflops": round(tflops, 1),
         "frac_of_peak": round(tflops / (peak_tf * world), 4),
         "frac_of_sustained_peak": round(tflops / (peak_sus * world), 4),
-        "frac_of_clock_limited_peak": _clock_frac(tflops / world, clocks),
+        "frac_of_clock_limited_peak": fwd_clock_frac,
+        "scaling_clock_normalised": scaling_cn,
         "peak_bf16_tflops": peak_tf,
         "peak_bf16_tflops_sustained": peak_sus,
         "peak_source": peaks.get("source"),
-        "roofline": {"bound": "tensor", "kernel": "gemm_tcgen05_kernel<CEPartialsEpilogue> (frx_fwd_partials)",
+        "roofline": {"bound": "tensor", "kernel": "gemm_tcgen05_pair_kernel<CEPartialsEpilogue> (frx_fwd_partials)",
                      "achieved": round(achieved_tflops, 1), "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": round(achieved_tflops / peak_tf, 4), "traffic": traffic,
                      "algorithmic_flop_per_launch": gemm_flops, "avg_launch_ms": round(gemm_avg_ms, 4),
@@ -582,10 +795,121 @@ def run_ours(args, world, rank, local):
         "accuracy": acc,
         "fwd_bwd": fb,
         "config0": small,
+        "configs": cfgs,
         "e2e": e2e,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
+
+
+def _clock_normalised_scaling(world, shape, fwd_frac, fb_frac):
+    """Each N's fraction of the clock-limited peak over the N=1 run's, for the forward and the training
+    step (per-GPU efficiency at equal clocks). The N=1 run stores its fractions on the box for the
+    N>1 runs that follow it; without that record the ratios are null."""
+    now = time.time()
+    if world == 1:
+        try:
+            _N1_STATE.write_text(json.dumps({"shape": list(shape), "fwd": fwd_frac, "fwd_bwd": fb_frac, "t": now}))
+        except OSError:
+            pass
+        return {"fwd": 1.0 if fwd_frac else None, "fwd_bwd": 1.0 if fb_frac else None,
+                "basis": "N=1 run of this command"}
+    try:
+        ref = json.loads(_N1_STATE.read_text())
+    except (OSError, ValueError):
+        return {"fwd": None, "fwd_bwd": None, "basis": "no N=1 record on this box"}
+    if ref.get("shape") != list(shape) or now - ref.get("t", 0) > 6 * 3600:
+        return {"fwd": None, "fwd_bwd": None, "basis": "no matching N=1 record on this box"}
+
+    def ratio(a, b):
+        return round(a / b, 4) if a and b else None
+
+    return {"fwd": ratio(fwd_frac, ref.get("fwd")), "fwd_bwd": ratio(fb_frac, ref.get("fwd_bwd")),
+            "basis": f"N=1 run {now - ref['t']:.0f} s earlier on this box"}
+
+
+def run_e2e(gk, vp, world, rank, local, hidden, weight, target, vstart, V, chunk, args):
+    """e2e: the public API with pinned host hidden / weight (shard) / target in and host results out.
+    With N ranks every rank uploads only its 1/N share of the hidden rows (the API's host path), so
+    only that share is pinned (cudaHostRegister on a pageable full-size tensor); host buffers are
+    allocated from CPUs of the GPU's NUMA node when the system reports one."""
+    B, H = hidden.shape
+    node = _gpu_numa_node(local)
+    cpus = _node_cpus(node) if node is not None else None
+    old_aff = None
+    if cpus:
+        try:
+            old_aff = os.sched_getaffinity(0)
+            os.sched_setaffinity(0, cpus)
+        except OSError:
+            old_aff = None
+    c = (B + world - 1) // world
+    lo, hi = min(B, rank * c), min(B, (rank + 1) * c)
+    registered = None
+    if world > 1:
+        h_host = torch.empty(B, H, dtype=hidden.dtype)
+        h_host[lo:hi].copy_(hidden[lo:hi])
+        try:
+            cr = torch.cuda.cudart()
+            nbytes = (hi - lo) * H * hidden.element_size()
+            if nbytes and int(cr.cudaHostRegister(h_host[lo:hi].data_ptr(), nbytes, 0)) == 0:
+                registered = h_host[lo:hi].data_ptr()
+        except Exception:
+            registered = None
+        if registered is None:  # fall back to pinning everything
+            h_host = h_host.pin_memory()
+    else:
+        h_host = torch.empty(B, H, dtype=hidden.dtype, pin_memory=True)
+        h_host.copy_(hidden)
+    w_host = torch.empty(weight.shape, dtype=weight.dtype, pin_memory=True)
+    w_host.copy_(weight)
+    t_host = torch.empty(target.shape, dtype=target.dtype, pin_memory=True)
+    t_host.copy_(target)
+
+    # This rank's H2D rate for its upload (hidden share + weight shard), all ranks at once.
+    up = hi - lo
+    dst_h = torch.empty(max(up, 1), H, dtype=hidden.dtype, device=hidden.device)
+    dst_w = torch.empty_like(weight)
+    barrier(world)
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_ev.record()
+    for _ in range(3):
+        if up:
+            dst_h[:up].copy_(h_host[lo:hi], non_blocking=True)
+        dst_w.copy_(w_host, non_blocking=True)
+    e_ev.record()
+    torch.cuda.synchronize()
+    up_bytes = (up * H + weight.numel()) * hidden.element_size()
+    gbs = up_bytes * 3 / (s_ev.elapsed_time(e_ev) / 1e3) / 1e9
+    del dst_h, dst_w
+    rates = torch.tensor([gbs], device=hidden.device, dtype=torch.float64)
+    if world > 1:
+        allr = torch.empty(world, device=hidden.device, dtype=torch.float64)
+        dist.all_gather_into_tensor(allr, rates)
+        rates = allr
+
+    def e2e_step():
+        if world == 1:
+            res = gk.gemm_fused_ce_entropy(h_host, w_host, t_host, chunk_size=chunk)
+        else:
+            res = vp.vocab_parallel_ce_entropy(h_host, w_host, t_host, vstart, V, chunk_size=chunk)
+        assert res[0].device.type == "cpu"
+
+    e2e_ms, _ = time_steps(e2e_step, max(1, min(args.steps, 10)), max(args.warmup, 3), world)
+    if registered is not None:
+        torch.cuda.cudart().cudaHostUnregister(registered)
+    if old_aff is not None:
+        os.sched_setaffinity(0, old_aff)
+    h2d = up * H * 2 + w_host.numel() * 2 + t_host.numel() * 8
+    return {"value": round(e2e_ms, 3), "unit": "ms", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(3 * B * 4),
+            "path": "pinned host hidden/weight(shard)/target -> gemm_fused_ce_entropy / vocab_parallel_ce_entropy "
+                    "(host in, host out; bytes per rank)",
+            "h2d_gbs_per_rank": [round(float(x), 1) for x in rates.tolist()],
+            "h2d_gbs_note": "each rank's own upload (hidden share + weight shard) copied alone, all ranks at once",
+            "numa": {"gpu_node": node, "host_buffers_bound_to_node": bool(cpus) and old_aff is not None,
+                     "hidden_pinned": "share only (cudaHostRegister)" if registered is not None else "whole tensor"}}
 
 
 def run_micro(args):
@@ -639,6 +963,14 @@ def run_micro(args):
     ms = timeit(lambda: ops.dlogits(z, tg, lse, ent, dz, rows=M, vocab_shard=V))
     report("dlogits", [M, V], ms, M * V * 6 + M * 16, "4 B logit read + 2 B dlogit write per element + row stats")
     del z
+    # the training pass's form: fp16 z - m_tile in, the tile maxima from the partials
+    T = ops.n_vocab_tiles(V)
+    zr = torch.randn(M, ops.round_up(V, 8), device=dev, generator=g).mul_(-3.0).to(torch.float16)
+    pt = torch.randn(T, M, 4, device=dev, generator=g)
+    ms = timeit(lambda: ops.dlogits_tilerel(zr, pt, M, tg, lse, ent, dz, rows=M, vocab_shard=V))
+    report("dlogits_tilerel", [M, V], ms, M * V * 4 + M * 16 + T * M * 4,
+           "2 B fp16 logit read + 2 B dlogit write per element + row stats + 4 B tile max per (tile, row)")
+    del zr, pt
 
     # column sums: d_bias of the headline training step (bf16 dlogits [32768, 128256] -> fp32 [V]).
     R2 = 32768 // sc
@@ -680,6 +1012,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-config0", action="store_true", help="skip the configs[0] eager-vs-graph line")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs[3] / configs[4] block")
+    ap.add_argument("--config-steps", type=int, default=3, help="timed steps per configs[3] / configs[4] leg")
     ap.add_argument("--micro", action="store_true", help="time the HBM-bound kernels alone (one line each)")
     ap.add_argument("--micro-scale", type=int, default=1, help="divide the --micro row counts (small ncu cases)")
     args = ap.parse_args()

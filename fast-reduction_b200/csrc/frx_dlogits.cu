@@ -38,17 +38,20 @@ __device__ __forceinline__ uint32_t pack_16x2(float lo, float hi, bool f16) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The fp16 value in the low (hi = false) or high half of `w` as a float.
+// The fp16 value in the low (hi = false) or high half of `w` as a float, with integer and FMA-pipe
+// instructions only: the magnitude bits moved into an fp32 exponent / mantissa and scaled by 2^112
+// (exact for every finite fp16, subnormals included), then the sign. A conversion instruction per
+// element would run on the same low-throughput unit as the exponential and made this HBM-bound
+// kernel compute-bound (3.2 TB/s at the headline shape). fp16 infinities come out as +-65536.
 __device__ __forceinline__ float half_of(uint32_t w, bool hi) {
-  __half h;
-  const uint16_t bits = static_cast<uint16_t>(hi ? (w >> 16) : (w & 0xFFFFu));
-  memcpy(&h, &bits, sizeof(h));
-  return __half2float(h);
+  const uint32_t h = hi ? (w >> 16) : w;
+  const float mag = __uint_as_float((h & 0x7FFFu) << 13) * 0x1p112f;
+  return __uint_as_float(__float_as_uint(mag) | ((h & 0x8000u) << 16));
 }
 
 // Tile-relative logits are stored saturated at the fp16 range: -inf (a logit more than 65504 below
-// its tile maximum) reads as -65504, whose probability is 0, so p * (a + b log p) stays 0 and
-// never becomes 0 * inf.
+// its tile maximum, read as -65536) is floored to -65504, whose probability is 0, so
+// p * (a + b log p) stays 0 and never becomes 0 * inf.
 constexpr float kRelFloor = -65504.0f;
 
 // kRel = false: `in` is fp32 logits z [rows, ld_in]. kRel = true: `in` is fp16 tile-relative

@@ -301,8 +301,10 @@ static int fwd_partials_impl(const void* hidden, int64_t ld_hidden, const void* 
   FRX_CHECK_RANGE(bias, vocab_shard * esz, "frx_fwd_partials: bias");
   FRX_CHECK_RANGE(target, rows * 8, "frx_fwd_partials: target");
   FRX_CHECK_RANGE(partials, matrix_bytes(n_tiles, rows, tile_stride, 16), "frx_fwd_partials: partials");
-  FRX_CHECK_RANGE(logits, matrix_bytes(rows, vocab_shard, ld_logits, 4), "frx_fwd_partials: logits");
-  FRX_CHECK_RANGE(zrel, matrix_bytes(rows, vocab_shard, ld_zrel, 2), "frx_fwd_partials_tilerel: logits_rel");
+  // The TMA stores write whole 16-byte chunks: each row's pad columns up to the next 16-byte boundary.
+  FRX_CHECK_RANGE(logits, matrix_bytes(rows, (vocab_shard + 3) / 4 * 4, ld_logits, 4), "frx_fwd_partials: logits");
+  FRX_CHECK_RANGE(zrel, matrix_bytes(rows, (vocab_shard + 7) / 8 * 8, ld_zrel, 2),
+                  "frx_fwd_partials_tilerel: logits_rel");
   CEPartialsEpilogue::Params ep;
   memset(&ep, 0, sizeof(ep));
   ep.n_tiles = static_cast<int>(n_tiles);

@@ -94,7 +94,10 @@ FRX_API const char* frx_last_error(void);
  *            reference's fp32 baseline computes; the reference's own GEMM path ignores bias)
  *   target   [rows] int64 global ids, or NULL (then zt = 0)
  *   partials [ceil(vocab_shard / 256) * tile_stride] x float4, tile_stride >= rows
- *   logits   optional fp32 [rows, ld_logits] output of every z (NULL: logits never leave the chip)
+ *   logits   optional fp32 [rows, ld_logits] output of every z (NULL: logits never leave the chip);
+ *            16-byte aligned, ld_logits a multiple of 4. The TMA stores write whole 16-byte chunks,
+ *            so the pad columns [vocab_shard, round_up(vocab_shard, 4)) of each row may be written
+ *            too: the buffer must extend to that column in its last row.
  */
 FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
                      int dtype, const void* bias, const int64_t* target, int64_t rows, int64_t vocab_shard,
@@ -113,7 +116,9 @@ FRX_API int frx_fwd_partials(const void* hidden, int64_t ld_hidden, const void* 
  * frx_dlogits_tilerel reads them back. Replaces, like the fp32 `logits` output of
  * frx_fwd_partials, the logits store of `_gemm_ce_entropy_bwd_kernel` (fast_reduction/gemm_kernel.py:168-273,
  * gemm_ce_entropy_bwd_epilogue.py:218), which writes fp32.
- *   logits_rel  fp16 [rows, ld_logits_rel], 16-byte aligned, ld_logits_rel a multiple of 8
+ *   logits_rel  fp16 [rows, ld_logits_rel], 16-byte aligned, ld_logits_rel a multiple of 8; the pad
+ *               columns [vocab_shard, round_up(vocab_shard, 8)) of each row may be written (whole
+ *               16-byte chunks), so the buffer must extend to that column in its last row
  */
 FRX_API int frx_fwd_partials_tilerel(const void* hidden, int64_t ld_hidden, const void* weight, int64_t ld_weight,
                                      int dtype, const void* bias, const int64_t* target, int64_t rows,

@@ -96,44 +96,46 @@ def test_invalid_arguments_return_codes_without_gpu():
     assert rc == nat.FRX_ERR_INVALID_ARG  # wait limit must be positive
 
 
-def test_integration_stub_matches_the_bindings():
-    """The ctypes stub INTEGRATION.md shows a maintainer declares the same argument types as the
-    package's own binding (fast_reduction/_native.py) for every entry point it lists."""
+def _stub_module():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("frx_ctypes_stub", REPO / "include" / "frx_ctypes.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_reference_side_stub_matches_the_bindings():
+    """include/frx_ctypes.py (the binding a maintainer adds to the reference package) declares, for
+    every entry point of include/frx.h, the same argument types as the package's own binding."""
     from fast_reduction import _native as nat
 
-    names = {"P": ctypes.c_void_p, "I64": ctypes.c_int64, "I32": ctypes.c_int, "F32": ctypes.c_float,
-             "ctypes.c_uint32": ctypes.c_uint32}
-    text = (REPO / "INTEGRATION.md").read_text()
-    stubs = re.findall(r"^_lib\.(frx_\w+)\.argtypes = \[([^\]]*)\]", text, flags=re.M)
-    assert len(stubs) >= 9
-    for fn, args in stubs:
-        declared = [names[a.strip()] for a in args.split(",")]
-        assert fn in nat.SIGNATURES, fn
-        assert declared == list(nat.SIGNATURES[fn][1]), fn
+    stub = _stub_module()
+    for name in declared_functions():
+        if name == "frx_last_error":
+            continue
+        assert name in stub.ARGTYPES, f"{name} missing from include/frx_ctypes.py"
+        assert list(stub.ARGTYPES[name]) == list(nat.SIGNATURES[name][1]), name
+    lib = stub.load(str(nat._LIB_PATH))
+    assert lib.frx_abi_version() == nat.load().frx_abi_version()
 
 
-def test_integration_calls_pass_every_argument():
-    """Every `_lib.frx_*(...)` call INTEGRATION.md shows passes as many arguments as the entry point
-    takes (top-level commas of the call, nested brackets skipped)."""
+def test_reference_side_stub_calls_pass_every_argument():
+    """Every `_lib.frx_*(...)` call in include/frx_ctypes.py passes as many arguments as the entry
+    point takes."""
+    import ast
+
     from fast_reduction import _native as nat
 
-    text = (REPO / "INTEGRATION.md").read_text()
+    tree = ast.parse((REPO / "include" / "frx_ctypes.py").read_text())
     seen = 0
-    for m in re.finditer(r"_lib\.(frx_\w+)\(", text):
-        depth, commas, j = 1, 0, m.end()
-        while depth:
-            c = text[j]
-            if c in "([":
-                depth += 1
-            elif c in ")]":
-                depth -= 1
-            elif c == "," and depth == 1:
-                commas += 1
-            j += 1
-        n_args = 0 if text[m.end():j - 1].strip() == "" else commas + 1
-        assert n_args == len(nat.SIGNATURES[m.group(1)][1]), m.group(1)
-        seen += 1
-    assert seen >= 8
+    for node in ast.walk(tree):
+        if (isinstance(node, ast.Call) and isinstance(node.func, ast.Attribute)
+                and isinstance(node.func.value, ast.Name) and node.func.value.id == "_lib"
+                and node.func.attr.startswith("frx_") and node.func.attr != "frx_last_error"):
+            assert len(node.args) == len(nat.SIGNATURES[node.func.attr][1]), node.func.attr
+            seen += 1
+    assert seen >= 13
 
 
 def test_last_error_is_per_thread():
