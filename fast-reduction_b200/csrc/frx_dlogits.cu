@@ -3,15 +3,23 @@
 //   p_j  = exp(z_j - lse)
 //   dz_j = p_j * (g_ce - g_ent * (log p_j + H)) - g_ce * [j == target]
 //
-// (reference: fast_reduction/cute_dlogits.py:87-100). Pure streaming kernel, HBM-bound:
-// reads fp32 logits once, writes bf16 (or fp16 / fp32) dlogits once. Each thread handles 16
-// consecutive columns of a row (four 16-byte streaming loads issued back to back, two 16-byte
-// 16-bit stores); the per-row constants A = g_ce - g_ent * H and B = -g_ent are formed once per
-// thread, after the loads are in flight.
+// (reference: fast_reduction/cute_dlogits.py:87-100). Pure streaming kernels, HBM-bound: they read
+// the logits once and write bf16 (or fp16 / fp32) dlogits once. Two inputs: fp32 logits z
+// (frx_dlogits), or fp16 tile-relative logits d = z - m_t with the tile maximum m_t taken from the
+// forward partials (frx_dlogits_tilerel, 2 bytes per logit read instead of 4); then
+// log p = d - (lse - m_t).
 //
-// Two inputs: fp32 logits z (frx_dlogits), or fp16 tile-relative logits d = z - m_t with the tile
-// maximum m_t taken from the forward partials (frx_dlogits_tilerel, 2 bytes per logit read instead
-// of 4). Then log p = d - (lse - m_t), and the rest is the same.
+// Layout: a warp owns whole rows of a column span; each lane covers 32 fp32 or 64 fp16 columns of
+// the row in 16-byte vectors placed so that consecutive lanes read consecutive 16 bytes (every load
+// is fully coalesced), all eight loads of the row are issued before any arithmetic (128 bytes in
+// flight per thread, 1024 threads per SM), and the per-row work (six constant loads, the target and
+// ignore test, the row pointer) is spread over those columns. Measured at the headline chunk
+// (4096 x 128256): one row and 16 columns per thread left the fp16 variant latency-bound at
+// 4.1 TB/s (32 bytes of loads in flight per thread); 8 columns per lane per row made both variants
+// issue-bound (25-30 instructions per logit, three of the four schedulers of every SM busy);
+// 32 fp16 columns per lane (64 bytes in flight) gave 4.6-5.0 TB/s. Neither staging the fp16 loads in
+// shared memory with LDGSTS two rows ahead (3.9 TB/s) nor a one-wave grid with L2 bulk prefetches
+// two rows ahead (3.5 TB/s fp16, 4.8 TB/s fp32) helped.
 #include <cstring>
 
 #include "frx_host.cuh"
@@ -19,142 +27,184 @@
 namespace frx {
 
 constexpr int kDlThreads = 256;
-constexpr int kDlVec = 16;  // columns per thread: four 16-byte loads in flight
-constexpr int kDlColsPerBlock = kDlThreads * kDlVec;
+constexpr int kDlWarps = kDlThreads / 32;
+// Four CTAs (1024 threads) per SM: the register cap (64) under which the loads in flight fit.
+constexpr int kDlMinBlocks = 4;
 
-// dz for one logit given lp = z - shift (shift = lse for fp32 logits, lse - m_t for tile-relative ones).
-__device__ __forceinline__ float dz_value(float z, float shift, float a, float b) {
-  const float lp = z - shift;
-  const float p = ex2_approx(lp * kLog2e);
-  return p * fmaf(b, lp, a);
-}
+// Per-lane shape: kVec elements per 16-byte load, kSlots loads per row at stride 32 * kVec columns
+// (the warp's loads of one slot are contiguous), one row per iteration. Either input keeps eight
+// 16-byte loads (128 bytes) in flight per thread: 32 fp32 or 64 fp16 columns per lane, a warp span of
+// 1024 or 2048 columns (four or eight vocabulary tiles).
+template <bool kRel>
+struct DlShape {
+  static constexpr int kVec = kRel ? 8 : 4;
+  static constexpr int kSlots = 8;
+  static constexpr int kSpan = 32 * kVec * kSlots;
+};
 
-__device__ __forceinline__ uint32_t pack_16x2(float lo, float hi, bool f16) {
-  if (f16) {
+// dz for one logit from lp = log p (p = exp(lp)): p * (a + b lp).
+__device__ __forceinline__ float dz_of(float lp, float a, float b) { return ex2_approx(lp * kLog2e) * fmaf(b, lp, a); }
+
+// Output element types of the kernels (template argument): bf16, fp16 or fp32.
+constexpr int kOutBf16 = 0, kOutF16 = 1, kOutF32 = 2;
+
+template <int kOut>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kOut == kOutF16) {
     __half2 h = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
   }
-  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The fp16 value in the low (hi = false) or high half of `w` as a float, with integer and FMA-pipe
-// instructions only: the magnitude bits moved into an fp32 exponent / mantissa and scaled by 2^112
-// (exact for every finite fp16, subnormals included), then the sign. A conversion instruction per
-// element would run on the same low-throughput unit as the exponential and made this HBM-bound
-// kernel compute-bound (3.2 TB/s at the headline shape). fp16 infinities come out as +-65536.
-__device__ __forceinline__ float half_of(uint32_t w, bool hi) {
-  const uint32_t h = hi ? (w >> 16) : w;
-  const float mag = __uint_as_float((h & 0x7FFFu) << 13) * 0x1p112f;
-  return __uint_as_float(__float_as_uint(mag) | ((h & 0x8000u) << 16));
+// Tile-relative logits d = z - m_t are never positive (m_t is the maximum of the tile's z), so an
+// fp16 d is decoded from its magnitude bits alone: moved into an fp32 exponent / mantissa they read
+// as |d| * 2^-112 (exact for every finite fp16, subnormals included), and the factor -2^112 is folded
+// into the FMA that forms log p = d - (lse - m_t). Two integer instructions per logit: an fp16
+// conversion instruction runs on the same low-throughput unit as the exponential and made this
+// kernel compute-bound (3.2 TB/s at the headline chunk), and a general decode with the sign took six.
+// fp16 -inf (a logit more than 65504 below its tile maximum) decodes to -65536, a finite value whose
+// probability is 0, so p * (a + b log p) stays 0 and never becomes 0 * inf.
+__device__ __forceinline__ float rel_mag(uint32_t w, bool hi) {
+  return __uint_as_float(hi ? ((w >> 3) & 0x0FFFE000u) : ((w << 13) & 0x0FFFE000u));
+}
+constexpr float kRelScale = -0x1p112f;
+
+// The per-row constants of the dz formula and the row's target column relative to the span
+// [cw, cw + span) (-1 when outside it).
+struct DlRow {
+  float a, b, gc_t, lse;
+  int tl;
+};
+
+__device__ __forceinline__ DlRow dl_row(int64_t row, int cw, int span, const int64_t* target, const float* lse,
+                                        const float* ent, const float* g_ce, const float* g_ent, float ce_weight,
+                                        float ent_weight, int64_t vocab_offset, int64_t ignore_index) {
+  const float gc = g_ce != nullptr ? g_ce[row] : ce_weight;
+  const float ge = g_ent != nullptr ? g_ent[row] : ent_weight;
+  DlRow r;
+  r.lse = lse[row];
+  r.tl = -1;
+  r.gc_t = gc;
+  if (target != nullptr) {
+    const int64_t t = target[row];
+    if (t == ignore_index) r.gc_t = 0.0f;  // CE term dropped for ignored rows; entropy term kept
+    const int64_t rel = t - vocab_offset - cw;
+    if (rel >= 0 && rel < span) r.tl = static_cast<int>(rel);
+  }
+  r.a = r.gc_t - ge * ent[row];
+  r.b = -ge;
+  return r;
 }
 
-// Tile-relative logits are stored saturated at the fp16 range: -inf (a logit more than 65504 below
-// its tile maximum, read as -65536) is floored to -65504, whose probability is 0, so
-// p * (a + b log p) stays 0 and never becomes 0 * inf.
-constexpr float kRelFloor = -65504.0f;
+// Writes the kVec dlogits d of one slot to o: one vector store when all are valid and the output
+// rows are 16-byte aligned, else element by element (n_valid of them).
+template <int kOut, int kVec>
+__device__ __forceinline__ void dl_store(void* o, const float (&d)[kVec], int n_valid, bool vec) {
+  if constexpr (kOut == kOutF32) {
+    float* of = static_cast<float*>(o);
+    if (vec && n_valid == kVec) {
+#pragma unroll
+      for (int i = 0; i < kVec; i += 4)
+        __stcs(reinterpret_cast<float4*>(of + i), make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < kVec; ++i)
+        if (i < n_valid) of[i] = d[i];
+    }
+  } else {
+    uint16_t* oh = static_cast<uint16_t*>(o);
+    if (vec && n_valid == kVec) {
+      uint32_t w[kVec / 2];
+#pragma unroll
+      for (int i = 0; i < kVec / 2; ++i) w[i] = pack2<kOut>(d[2 * i], d[2 * i + 1]);
+      if constexpr (kVec == 8)
+        __stcs(reinterpret_cast<uint4*>(oh), make_uint4(w[0], w[1], w[2], w[3]));
+      else
+        __stcs(reinterpret_cast<uint2*>(oh), make_uint2(w[0], w[1]));
+    } else {
+#pragma unroll
+      for (int i = 0; i < kVec; ++i)
+        if (i < n_valid) oh[i] = static_cast<uint16_t>(pack2<kOut>(d[i], 0.0f) & 0xFFFFu);
+    }
+  }
+}
 
-// kRel = false: `in` is fp32 logits z [rows, ld_in]. kRel = true: `in` is fp16 tile-relative
-// logits d = z - m_t [rows, ld_in], and m_t is slot 0 of partials[t * tile_stride + row] for the
-// 256-column tile t of the column.
-template <bool kRel>
-__global__ void __launch_bounds__(kDlThreads)
+// kRel = false: `in` is fp32 logits z [rows, ld_in]. kRel = true: `in` is fp16 tile-relative logits
+// d = z - m_t <= 0 [rows, ld_in], and m_t is slot 0 of partials[t * tile_stride + row] for the
+// 256-column tile t of the column. kOut: the dlogits type. Column indices are 32-bit
+// (vocab_shard < 2^31 - span). in_vec / out_vec: rows 16-byte aligned (vector loads / stores).
+template <bool kRel, int kOut>
+__global__ void __launch_bounds__(kDlThreads, kDlMinBlocks)
     dlogits_kernel(const void* __restrict__ in, int64_t ld_in, const float4* __restrict__ partials,
                    int64_t tile_stride, const int64_t* __restrict__ target, const float* __restrict__ lse,
                    const float* __restrict__ ent, const float* __restrict__ g_ce, const float* __restrict__ g_ent,
-                   float ce_weight, float ent_weight, void* __restrict__ out, int64_t ld_out, int out_f32,
-                   int out_f16, int64_t rows, int64_t cols, int64_t vocab_offset, int64_t ignore_index, int vec_ok) {
-  const int64_t c0 = (static_cast<int64_t>(blockIdx.x) * kDlThreads + threadIdx.x) * kDlVec;
-  if (c0 >= cols) return;
-  const bool full = vec_ok && c0 + kDlVec <= cols;
-  const int64_t tile = c0 / FRX_VOCAB_TILE;  // kDlVec divides the tile width: one tile per thread
-  for (int64_t row = blockIdx.y; row < rows; row += gridDim.y) {
-    float z[kDlVec];
-    if (kRel) {
-      const uint16_t* zrow = static_cast<const uint16_t*>(in) + row * ld_in;
-      if (full) {
+                   float ce_weight, float ent_weight, void* __restrict__ out, int64_t ld_out, int64_t rows, int cols,
+                   int64_t vocab_offset, int64_t ignore_index, int in_vec, int out_vec) {
+  using S = DlShape<kRel>;
+  constexpr int kVec = S::kVec, kSlots = S::kSlots;
+  constexpr int kInBytes = kRel ? 2 : 4;
+  constexpr int kOutBytes = kOut == kOutF32 ? 4 : 2;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int cw = blockIdx.x * S::kSpan;
+  const int c0 = cw + lane * kVec;  // this lane's first column; slot s starts 32 * kVec * s further
+  const int64_t row_step = static_cast<int64_t>(gridDim.y) * kDlWarps;
+  for (int64_t row = static_cast<int64_t>(blockIdx.y) * kDlWarps + warp; row < rows; row += row_step) {
+    const char* rp = static_cast<const char*>(in) + row * ld_in * kInBytes;
+    // All loads of the row first.
+    uint4 raw[kSlots];
 #pragma unroll
-        for (int i = 0; i < kDlVec; i += 8) {
-          const uint4 q = __ldcs(reinterpret_cast<const uint4*>(zrow + c0 + i));
-          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    for (int s = 0; s < kSlots; ++s) {
+      const int c = c0 + s * 32 * kVec;
+      raw[s] = make_uint4(0u, 0u, 0u, 0u);
+      if (in_vec && c + kVec <= cols) raw[s] = __ldcs(reinterpret_cast<const uint4*>(rp + c * kInBytes));
+    }
+    const DlRow r = dl_row(row, cw, S::kSpan, target, lse, ent, g_ce, g_ent, ce_weight, ent_weight, vocab_offset,
+                           ignore_index);
+    // tile maximum of this lane's first slot (kRel: one 256-column tile per slot)
+    const float4* pm = partials + static_cast<int64_t>(c0 / FRX_VOCAB_TILE) * tile_stride + row;
+    char* op = static_cast<char*>(out) + row * ld_out * kOutBytes;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            z[i + 2 * j] = half_of(w[j], false);
-            z[i + 2 * j + 1] = half_of(w[j], true);
-          }
+    for (int s = 0; s < kSlots; ++s) {
+      const int c = c0 + s * 32 * kVec;
+      const int nv = min(cols - c, kVec);  // valid columns of this slot
+      if (nv <= 0) continue;
+      float lp[kVec];
+      if constexpr (kRel) {
+        const float nshift = __ldg(&pm[s * tile_stride].x) - r.lse;  // -(lse - m_t)
+        if (in_vec && nv == kVec) {
+          const uint32_t w[4] = {raw[s].x, raw[s].y, raw[s].z, raw[s].w};
+#pragma unroll
+          for (int i = 0; i < kVec; ++i) lp[i] = fmaf(rel_mag(w[i >> 1], (i & 1) != 0), kRelScale, nshift);
+        } else {
+#pragma unroll
+          for (int i = 0; i < kVec; ++i)
+            lp[i] = i < nv ? fmaf(rel_mag(reinterpret_cast<const uint16_t*>(rp)[c + i], false), kRelScale, nshift)
+                           : 0.0f;
         }
       } else {
+        if (in_vec && nv == kVec) {
+          const uint32_t w[4] = {raw[s].x, raw[s].y, raw[s].z, raw[s].w};
 #pragma unroll
-        for (int i = 0; i < kDlVec; ++i) z[i] = (c0 + i < cols) ? half_of(zrow[c0 + i], false) : 0.0f;
-      }
+          for (int i = 0; i < kVec; ++i) lp[i] = __uint_as_float(w[i]) - r.lse;
+        } else {
 #pragma unroll
-      for (int i = 0; i < kDlVec; ++i) z[i] = fmaxf(z[i], kRelFloor);
-    } else {
-      const float* zrow = static_cast<const float*>(in) + row * ld_in;
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < kDlVec; i += 4) {
-          const float4 q = __ldcs(reinterpret_cast<const float4*>(zrow + c0 + i));
-          z[i] = q.x;
-          z[i + 1] = q.y;
-          z[i + 2] = q.z;
-          z[i + 3] = q.w;
+          for (int i = 0; i < kVec; ++i) lp[i] = i < nv ? reinterpret_cast<const float*>(rp)[c + i] - r.lse : 0.0f;
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kDlVec; ++i) z[i] = (c0 + i < cols) ? zrow[c0 + i] : 0.0f;
       }
-    }
-    const float gc = g_ce != nullptr ? g_ce[row] : ce_weight;
-    const float ge = g_ent != nullptr ? g_ent[row] : ent_weight;
-    const float row_lse = kRel ? lse[row] - __ldg(&partials[tile * tile_stride + row].x) : lse[row];
-    const float h = ent[row];
-    int64_t tcol = -1;
-    float gc_t = gc;
-    if (target != nullptr) {
-      const int64_t t = target[row];
-      if (t == ignore_index) gc_t = 0.0f;  // CE term dropped for ignored rows; entropy term kept
-      tcol = t - vocab_offset;
-    }
-    const float a = gc_t - ge * h;
-    const float b = -ge;
-    float d[kDlVec];
+      float d[kVec];
 #pragma unroll
-    for (int i = 0; i < kDlVec; ++i) d[i] = dz_value(z[i], row_lse, a, b);
-    if (tcol >= c0 && tcol < c0 + kDlVec) {
+      for (int i = 0; i < kVec; ++i) d[i] = dz_of(lp[i], r.a, r.b);
+      const int hit = r.tl - (c - cw);
+      if (hit >= 0 && hit < kVec) {
 #pragma unroll
-      for (int i = 0; i < kDlVec; ++i)
-        if (c0 + i == tcol) d[i] -= gc_t;
-    }
-    if (out_f32) {
-      float* orow = static_cast<float*>(out) + row * ld_out;
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < kDlVec; i += 4)
-          __stcs(reinterpret_cast<float4*>(orow + c0 + i), make_float4(d[i], d[i + 1], d[i + 2], d[i + 3]));
-      } else {
-#pragma unroll
-        for (int i = 0; i < kDlVec; ++i)
-          if (c0 + i < cols) orow[c0 + i] = d[i];
+        for (int i = 0; i < kVec; ++i)
+          if (i == hit) d[i] -= r.gc_t;
       }
-    } else {
-      const bool f16 = out_f16 != 0;
-      uint16_t* orow = static_cast<uint16_t*>(out) + row * ld_out;
-      if (full) {
-#pragma unroll
-        for (int i = 0; i < kDlVec; i += 8) {
-          uint4 pk;
-          pk.x = pack_16x2(d[i], d[i + 1], f16);
-          pk.y = pack_16x2(d[i + 2], d[i + 3], f16);
-          pk.z = pack_16x2(d[i + 4], d[i + 5], f16);
-          pk.w = pack_16x2(d[i + 6], d[i + 7], f16);
-          __stcs(reinterpret_cast<uint4*>(orow + c0 + i), pk);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kDlVec; ++i)
-          if (c0 + i < cols) orow[c0 + i] = static_cast<uint16_t>(pack_16x2(d[i], 0.0f, f16) & 0xFFFFu);
-      }
+      dl_store<kOut, kVec>(op + static_cast<int64_t>(c) * kOutBytes, d, nv, out_vec != 0);
     }
   }
 }
@@ -185,8 +235,8 @@ static int dlogits_impl(bool rel, const char* name, const void* in, int64_t ld_i
   const int out_f16 = out_dtype == FRX_DTYPE_F16 ? 1 : 0;
   const int64_t out_elem = out_f32 ? 4 : 2;
   const int64_t in_elem = rel ? 2 : 4;
-  const int vec_ok = aligned16(in) && aligned16(dlogits) && ((ld_in * in_elem) % 16 == 0) &&
-                     ((ld_dlogits * out_elem) % 16 == 0);
+  const int in_vec = aligned16(in) && ((ld_in * in_elem) % 16 == 0) ? 1 : 0;
+  const int out_vec = aligned16(dlogits) && ((ld_dlogits * out_elem) % 16 == 0) ? 1 : 0;
   [[maybe_unused]] const int64_t n_tiles = (vocab_shard + FRX_VOCAB_TILE - 1) / FRX_VOCAB_TILE;
   FRX_CHECK_RANGE(in, matrix_bytes(rows, vocab_shard, ld_in, in_elem), "dlogits: logits");
   FRX_CHECK_RANGE(partials, rel ? matrix_bytes(n_tiles, rows, tile_stride, 16) : 0, "dlogits: partials");
@@ -196,14 +246,21 @@ static int dlogits_impl(bool rel, const char* name, const void* in, int64_t ld_i
   FRX_CHECK_RANGE(entropy, rows * 4, "dlogits: entropy");
   FRX_CHECK_RANGE(g_ce, rows * 4, "dlogits: g_ce");
   FRX_CHECK_RANGE(g_ent, rows * 4, "dlogits: g_ent");
-  const int64_t gx = (vocab_shard + kDlColsPerBlock - 1) / kDlColsPerBlock;
-  FRX_REQUIRE(gx < (1ll << 31), FRX_ERR_INVALID_ARG, "%s: vocab_shard too large", name);
-  const unsigned gy = static_cast<unsigned>(rows < 65535 ? rows : 65535);
-  dim3 grid(static_cast<unsigned>(gx), gy);
-  auto kernel = rel ? dlogits_kernel<true> : dlogits_kernel<false>;
-  kernel<<<grid, kDlThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+  const int span = rel ? DlShape<true>::kSpan : DlShape<false>::kSpan;
+  FRX_REQUIRE(vocab_shard < (1ll << 31) - span, FRX_ERR_INVALID_ARG, "%s: vocab_shard too large", name);
+  const int cols = static_cast<int>(vocab_shard);
+  const int64_t gx = (vocab_shard + span - 1) / span;
+  const int64_t row_blocks = (rows + kDlWarps - 1) / kDlWarps;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned gy = static_cast<unsigned>(row_blocks < 65535 ? row_blocks : 65535);
+  const int okind = out_f32 ? kOutF32 : (out_f16 ? kOutF16 : kOutBf16);
+  auto kernel = rel ? (okind == kOutF32 ? dlogits_kernel<true, kOutF32>
+                       : okind == kOutF16 ? dlogits_kernel<true, kOutF16> : dlogits_kernel<true, kOutBf16>)
+                    : (okind == kOutF32 ? dlogits_kernel<false, kOutF32>
+                       : okind == kOutF16 ? dlogits_kernel<false, kOutF16> : dlogits_kernel<false, kOutBf16>);
+  kernel<<<dim3(static_cast<unsigned>(gx), gy), kDlThreads, 0, st>>>(
       in, ld_in, reinterpret_cast<const float4*>(partials), tile_stride, target, lse, entropy, g_ce, g_ent, ce_weight,
-      ent_weight, dlogits, ld_dlogits, out_f32, out_f16, rows, vocab_shard, vocab_offset, ignore_index, vec_ok);
+      ent_weight, dlogits, ld_dlogits, rows, cols, vocab_offset, ignore_index, in_vec, out_vec);
   FRX_CUDA_CHECK(cudaGetLastError());
   return FRX_OK;
 }

@@ -160,7 +160,9 @@ FRX_API int frx_dlogits(const float* logits, int64_t ld_logits, const int64_t* t
  * frx_dlogits from the fp16 tile-relative logits of frx_fwd_partials_tilerel and the partials of the
  * same launch (tile maximum m_t in slot 0 of partials[t * tile_stride + r]):
  *   log p = max(logits_rel, -65504) - (lse - m_t),  dz = p * (g_ce - g_ent * (log p + H)) - g_ce * [j == target]
- * Reads 2 bytes per logit instead of 4. Same arguments and rules as frx_dlogits otherwise.
+ * Reads 2 bytes per logit instead of 4. The values are z minus the maximum of their tile, so never
+ * positive: the kernel decodes them from their magnitude bits (a positive value would be read as
+ * its negation). Same arguments and rules as frx_dlogits otherwise.
  * Replaces `ComputeDlogits` / `compute_dlogits` (fast_reduction/cute_dlogits.py:32-100, 162-183)
  * in the training pass.
  */

@@ -97,8 +97,9 @@ def _rand_case(M, V, seed, with_neg_inf=False):
     return m.float(), d16, zf, lse, ent
 
 
-@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
-def test_dlogits_tilerel_matches_oracle(out_dtype):
+@pytest.mark.parametrize("out_dtype,aligned", [(torch.float32, True), (torch.bfloat16, True), (torch.float16, True),
+                                               (torch.bfloat16, False)])
+def test_dlogits_tilerel_matches_oracle(out_dtype, aligned):
     from fast_reduction import ops
 
     M, V, off = 70, 1003, 500
@@ -110,7 +111,10 @@ def test_dlogits_tilerel_matches_oracle(out_dtype):
     gce = torch.rand(M, generator=g)
     gent = torch.randn(M, generator=g)
     ld = 1008
-    rel = torch.zeros(M, ld, device=DEV, dtype=torch.float16)
+    if aligned:
+        rel = torch.zeros(M, ld, device=DEV, dtype=torch.float16)
+    else:  # rows start 2 bytes past a 16-byte boundary: the element-wise load path
+        rel = torch.zeros(M, ld + 1, device=DEV, dtype=torch.float16)[:, 1:]
     rel[:, :V] = d16.to(DEV)
     T = m.shape[0]
     part = torch.zeros(T, M, 4, device=DEV)
