@@ -9,8 +9,10 @@ rank) and merges them with the same associative rule as the per-tile merge
 full ce / entropy / lse.
 
 Training: dlogits and d_weight of a slice are local; d_hidden is a sum over slices. Each rank
-computes its partial d_hidden in fp32 and one NCCL all-reduce on a side stream, overlapped with the
-d_weight GEMM, completes it. An alternative (FRX_NVLS=1) fuses the sum into the d_hidden GEMM: its
+computes its partial d_hidden in fp32; on a side stream, overlapped with the d_weight GEMM, an NCCL
+reduce-scatter sums every rank's share of the rows, the share is cast to the hidden dtype, and an
+all-gather assembles d_hidden on every rank (FRX_DH_COLLECTIVE=allreduce: one fp32 all-reduce and a
+full-size cast instead). An alternative (FRX_NVLS=1) fuses the sum into the d_hidden GEMM: its
 epilogue adds every finished fp32 tile into all ranks' copies of a symmetric-memory buffer through
 the NVSwitch (`frx_gemm_dhidden_multicast`, multimem.red). It is correct but slower on B200 at this
 volume (512 MiB of reductions per rank: the fused GEMM took 13.5 ms vs 11.5 ms + overlapped NCCL at
@@ -34,6 +36,11 @@ from . import ops
 
 # FRX_NVLS=1 selects the multicast-fused d_hidden reduction (when the GPUs support NVLS).
 _USE_NVLS = os.environ.get("FRX_NVLS", "0") == "1"
+_DH_COLLECTIVE = os.environ.get("FRX_DH_COLLECTIVE", "rs_ag")
+# The d_hidden sum over ranks: "rs_ag" (default) reduce-scatters the fp32 contributions, casts this
+# rank's rows to the hidden dtype and all-gathers them into d_hidden (25% fewer bytes over NVLink
+# than an fp32 all-reduce, and no full-size cast afterwards); "allreduce" sums the whole fp32 matrix
+# on every rank and casts it (for A/B measurement).
 _nvls_buffers: dict = {}
 
 
@@ -170,12 +177,23 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
             for a_op, b_op in pairs:  # multimem.red adds every product into every rank's copy
                 ops.gemm_dhidden_multicast(a_op, b_op, hdl.multicast_ptr, H, rows=B, vocab_shard=Vr, device=dev)
             return None, None
-    else:
+    elif _DH_COLLECTIVE == "allreduce":
         def dhidden_fn(pairs):
             dh = torch.empty(B, H, device=dev, dtype=torch.float32)
             for i, (a_op, b_op) in enumerate(pairs):
                 ops.gemm_dhidden(a_op, b_op, dh, rows=B, vocab_shard=Vr, accumulate=i > 0)
             return dh, _allreduce_async(dh, group)
+    else:
+        world = dist.get_world_size(group)
+        share = (B + world - 1) // world
+
+        def dhidden_fn(pairs):
+            # [world * share, H] so that reduce-scatter hands every rank `share` rows; the padded rows
+            # past B are never written and only ever reach the padded rows of the result
+            dh = torch.empty(world * share, H, device=dev, dtype=torch.float32)
+            for i, (a_op, b_op) in enumerate(pairs):
+                ops.gemm_dhidden(a_op, b_op, dh, rows=B, vocab_shard=Vr, accumulate=i > 0)
+            return None, _reduce_scatter_gather_async(dh, share, hidden_2d.dtype, group)
 
     d_hidden_f32, d_weight, d_bias, pending = gk.fwd_bwd_shard(
         hidden_2d, weight_shard, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
@@ -186,12 +204,15 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
         hdl.barrier()  # every rank's reductions have landed in every copy
         return ce, ent, buf.to(hidden_2d.dtype), d_weight, d_bias
     pending.wait_into_current()
+    if d_hidden_f32 is None:  # reduce-scatter + all-gather: already summed and in the hidden dtype
+        return ce, ent, pending.result[:B], d_weight, d_bias
     return ce, ent, d_hidden_f32.to(hidden_2d.dtype), d_weight, d_bias
 
 
 class _PendingAllReduce:
-    def __init__(self, event: torch.cuda.Event):
+    def __init__(self, event: torch.cuda.Event, result: Optional[Tensor] = None):
         self.event = event
+        self.result = result
 
     def wait_into_current(self):
         torch.cuda.current_stream().wait_event(self.event)
@@ -216,6 +237,40 @@ def _allreduce_async(t: Tensor, group) -> _PendingAllReduce:
         done.record(side)
     t.record_stream(side)
     return _PendingAllReduce(done)
+
+
+def _reduce_scatter_gather_async(dh32: Tensor, share: int, dtype: torch.dtype, group) -> _PendingAllReduce:
+    """Sum of every rank's fp32 [world * share, H] contribution, in `dtype`, on a side stream (so it
+    overlaps the caller's next kernel, the d_weight GEMM): reduce-scatter in fp32 (this rank gets
+    rows [rank * share, (rank + 1) * share) summed), cast of those rows (bf16: libfrx's round to
+    nearest, the hi part of frx_split_f32), all-gather of the casts. Returns a handle whose wait
+    orders the caller's stream after it and whose `result` is the [world * share, H] sum."""
+    dev = dh32.device.index
+    side = _side_streams.get(dev)
+    if side is None:
+        side = torch.cuda.Stream(device=dh32.device)
+        _side_streams[dev] = side
+    H = dh32.shape[1]
+    world = dh32.shape[0] // share
+    main = torch.cuda.current_stream()
+    side.wait_stream(main)
+    with torch.cuda.stream(side), ops.phase("frx.vp.dhidden_reduce_scatter_gather"):
+        part32 = torch.empty(share, H, device=dh32.device, dtype=torch.float32)
+        dist.reduce_scatter_tensor(part32, dh32, op=dist.ReduceOp.SUM, group=group)
+        if dtype == torch.float32:
+            part = part32
+        elif dtype == torch.bfloat16:
+            part = torch.empty(share, H, device=dh32.device, dtype=torch.bfloat16)
+            ops.split_f32(part32, part, (ops.nat.FRX_PART_HI,), part_stride=0)
+        else:
+            part = part32.to(dtype)
+        out = torch.empty(world * share, H, device=dh32.device, dtype=dtype)
+        dist.all_gather_into_tensor(out, part, group=group)
+        done = torch.cuda.Event()
+        done.record(side)
+    for t in (dh32, part32, part, out):
+        t.record_stream(side)
+    return _PendingAllReduce(done, out)
 
 
 class VocabParallelMegakernel(torch.autograd.Function):

@@ -17,7 +17,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q, nvls, dtype_name="bfloat16"):
+def _worker(rank, world, port, q, nvls, dtype_name="bfloat16", dh_collective="rs_ag"):
     try:
         import datetime
         import os
@@ -25,6 +25,7 @@ def _worker(rank, world, port, q, nvls, dtype_name="bfloat16"):
         from pathlib import Path
 
         os.environ["FRX_NVLS"] = "1" if nvls else "0"  # read when fast_reduction.vocab_parallel is imported
+        os.environ["FRX_DH_COLLECTIVE"] = dh_collective
         repo = Path(__file__).resolve().parents[1]
         for p in (str(repo / "fast-reduction_b200"), str(repo)):
             if p not in sys.path:
@@ -82,18 +83,21 @@ def _worker(rank, world, port, q, nvls, dtype_name="bfloat16"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs at least two GPUs")
-@pytest.mark.parametrize("nvls,dtype_name", [(True, "bfloat16"), (False, "bfloat16"), (False, "float16"),
-                                             (False, "float32")],
-                         ids=["nvls-fused-dhidden", "nccl-allreduce", "nccl-fp16", "nccl-fp32"])
-def test_vocab_parallel_matches_single_gpu(nvls, dtype_name):
-    """Both d_hidden reductions: the NCCL all-reduce (default) and the reduction fused into the GEMM
-    through NVLS multicast (FRX_NVLS=1; when the GPUs lack NVLS this case runs the NCCL path too);
-    fp16 and fp32 operands on the default path."""
+@pytest.mark.parametrize("nvls,dtype_name,dh_collective", [
+    (True, "bfloat16", "rs_ag"), (False, "bfloat16", "rs_ag"), (False, "bfloat16", "allreduce"),
+    (False, "float16", "rs_ag"), (False, "float32", "rs_ag")],
+    ids=["nvls-fused-dhidden", "nccl-rs-ag", "nccl-allreduce", "nccl-fp16", "nccl-fp32"])
+def test_vocab_parallel_matches_single_gpu(nvls, dtype_name, dh_collective):
+    """The d_hidden reductions: NCCL reduce-scatter + cast + all-gather (default), one NCCL fp32
+    all-reduce (FRX_DH_COLLECTIVE=allreduce), and the reduction fused into the GEMM through NVLS
+    multicast (FRX_NVLS=1; when the GPUs lack NVLS this case runs the default path); fp16 and fp32
+    operands on the default path. B = 520 rows do not split evenly over 4 ranks' shares."""
     world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, nvls, dtype_name)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, nvls, dtype_name, dh_collective))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
