@@ -228,10 +228,11 @@ extern "C" int frx_gemm_dhidden(const void* dlogits, int64_t ld_dlogits, const v
                                                  status, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
-                                int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
-                                int64_t hidden_dim, int64_t rows, int* status, void* stream) {
-  using namespace frx;
+namespace frx {
+
+static int gemm_dweight_impl(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
+                             int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
+                             int64_t hidden_dim, int64_t rows, int max_sms, int* status, void* stream) {
   FRX_REQUIRE(rows >= 1 && hidden_dim >= 1 && vocab_shard >= 0 && rows < (1ll << 31) && hidden_dim < (1ll << 31) &&
                   vocab_shard < (1ll << 31),
               FRX_ERR_INVALID_ARG, "frx_gemm_dweight: bad sizes rows=%lld hidden_dim=%lld vocab_shard=%lld",
@@ -248,7 +249,25 @@ extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const v
   Operand b{hidden, ld_hidden, hidden_dim, rows, true, in_dtype};     // [rows, H] row-major, N = H contiguous
   return launch_gemm<true, true, true, StoreEpilogue>(a, b, vocab_shard, hidden_dim, rows, 8,
                                                 store_params(d_weight, ld_d_weight, vocab_shard, hidden_dim, out_dtype),
-                                                status, static_cast<cudaStream_t>(stream));
+                                                status, static_cast<cudaStream_t>(stream), -1, kWaitLimitNs, max_sms);
+}
+
+}  // namespace frx
+
+extern "C" int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
+                                int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype, int64_t vocab_shard,
+                                int64_t hidden_dim, int64_t rows, int* status, void* stream) {
+  return frx::gemm_dweight_impl(dlogits, ld_dlogits, hidden, ld_hidden, in_dtype, d_weight, ld_d_weight, out_dtype,
+                                vocab_shard, hidden_dim, rows, 0, status, stream);
+}
+
+extern "C" int frx_gemm_dweight_sms(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
+                                    int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype,
+                                    int64_t vocab_shard, int64_t hidden_dim, int64_t rows, int max_sms, int* status,
+                                    void* stream) {
+  FRX_REQUIRE(max_sms >= 0, FRX_ERR_INVALID_ARG, "frx_gemm_dweight_sms: max_sms %d < 0", max_sms);
+  return frx::gemm_dweight_impl(dlogits, ld_dlogits, hidden, ld_hidden, in_dtype, d_weight, ld_d_weight, out_dtype,
+                                vocab_shard, hidden_dim, rows, max_sms, status, stream);
 }
 
 extern "C" int frx_gemm_dhidden_multicast(const void* dlogits, int64_t ld_dlogits, const void* weight,

@@ -150,10 +150,12 @@ int max_pair_clusters(Kernel kernel, std::atomic<int>* cache, int smem_bytes, in
 
 // Launches the GEMM core. kWide selects 256 x 512 pair tiles (backward GEMMs, long K) instead of
 // 256 x 256 double-buffered tiles (forward); it only applies to the pair kernel.
+// max_sms > 0 caps the persistent grid at that many SMs (the others stay free for concurrent work,
+// e.g. a collective on another stream); 0 uses every SM.
 template <bool kAMN, bool kBMN, bool kWide, class Epi>
 int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_t K, int group_m,
                 const typename Epi::Params& ep, int* status, cudaStream_t stream, int stall_kb = -1,
-                uint64_t wait_limit_ns = kWaitLimitNs) {
+                uint64_t wait_limit_ns = kWaitLimitNs, int max_sms = 0) {
   FRX_REQUIRE(is_gemm_dtype(a.dtype) && a.dtype == b.dtype, FRX_ERR_INVALID_ARG,
               "GEMM operands must both be bf16 or both fp16 (dtype codes %d, %d)", a.dtype, b.dtype);
   const bool pair = use_pair_kernel();
@@ -191,6 +193,7 @@ int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_
     int clusters = 0;
     rc = max_pair_clusters(kernel, clusters_cache, smem, &clusters);
     if (rc) return rc;
+    if (max_sms > 0 && max_sms / 2 < clusters) clusters = max_sms / 2 < 1 ? 1 : max_sms / 2;
     const long long pairs = tiles < clusters ? tiles : clusters;
     kernel<<<static_cast<unsigned>(2 * pairs), kGemmThreads, smem, stream>>>(tm_a, tm_b, sched, num_k_blocks, ep,
                                                                              status);
@@ -205,6 +208,7 @@ int launch_gemm(const Operand& a, const Operand& b, int64_t M, int64_t N, int64_
     int sms = 0;
     rc = sm_count(&sms);
     if (rc) return rc;
+    if (max_sms > 0 && max_sms < sms) sms = max_sms;
     const int grid = static_cast<int>(tiles < sms ? tiles : sms);
     kernel<<<grid, kGemmThreads, smem, stream>>>(tm_a, tm_b, sched, num_k_blocks, ep, status);
   }

@@ -77,6 +77,7 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "frx_gemm_dhidden": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
     "frx_gemm_dweight": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I32, _I64, _I64, _I64, _P, _P]),
+    "frx_gemm_dweight_sms": (_I32, [_P, _I64, _P, _I64, _I32, _P, _I64, _I32, _I64, _I64, _I64, _I32, _P, _P]),
     "frx_fwd_ce_entropy_noalloc": (_I32, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _P, _P, _P, _P, _P, _P]),
     "frx_logits_partials": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _I64, _P, _I64, _P]),
     "frx_column_sums": (_I32, [_P, _I32, _I64, _I64, _I64, _P, _P]),

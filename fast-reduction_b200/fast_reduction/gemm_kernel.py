@@ -582,6 +582,7 @@ def fwd_bwd_shard(
     dhidden_fn=None,
     bias: Optional[Tensor] = None,
     vocab_size: Optional[int] = None,
+    dweight_max_sms: int = 0,
 ):
     """Training pass over one vocabulary shard; returns (d_hidden, d_weight [V_shard, H],
     d_bias [V_shard] or None, pending).
@@ -600,7 +601,8 @@ def fwd_bwd_shard(
     (single GPU: a local finalize; vocabulary-parallel: local merge + cross-rank exchange), which
     runs on the side stream with the launch's dlogits when there are several launches; the
     dlogits kernel writes the launch's dlogits (in the operands' 16-bit type) into a [B, V_shard]
-    buffer. Then one d_hidden GEMM and one d_weight GEMM over all rows.
+    buffer. Then one d_hidden GEMM and one d_weight GEMM over all rows (on at most ``dweight_max_sms``
+    SMs when it is positive, so a collective started by ``dhidden_fn`` can run beside it).
     """
     B, H = hidden_2d.shape
     V = weight.shape[0]
@@ -707,9 +709,10 @@ def fwd_bwd_shard(
             del w_parts, dh_pairs
             x_parts = _fp32_parts(hidden_2d)
             for n_, (i, j) in enumerate(zip(ops.SPLIT_LEFT, ops.SPLIT_RIGHT)):
-                ops.gemm_dweight(dz_parts[i], x_parts[j], d_weight, rows=B, vocab_shard=V, accumulate=n_ > 0)
+                ops.gemm_dweight(dz_parts[i], x_parts[j], d_weight, rows=B, vocab_shard=V, accumulate=n_ > 0,
+                                 max_sms=dweight_max_sms)
         else:
-            ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V)
+            ops.gemm_dweight(dz, hidden_2d, d_weight, rows=B, vocab_shard=V, max_sms=dweight_max_sms)
     d_bias = None
     if bias is not None:
         d_bias32 = torch.empty(V, device=dev, dtype=torch.float32)

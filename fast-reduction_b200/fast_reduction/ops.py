@@ -360,8 +360,9 @@ def gemm_dhidden(dz: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, *, r
 
 
 def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, rows: int, vocab_shard: int,
-                 accumulate: bool = False) -> None:
-    """out[vocab_shard, H] <- dz[rows, vocab_shard]^T @ hidden[rows, H] (``accumulate``: fp32 out +=)."""
+                 accumulate: bool = False, max_sms: int = 0) -> None:
+    """out[vocab_shard, H] <- dz[rows, vocab_shard]^T @ hidden[rows, H] (``accumulate``: fp32 out +=), on at
+    most ``max_sms`` SMs when it is positive (frx_gemm_dweight_sms)."""
     dev = _require_cuda(dz, hidden, out)
     dt = _gemm_dtype(dz, hidden)
     ldz = _row_major(dz, "dz")
@@ -371,6 +372,13 @@ def gemm_dweight(dz: torch.Tensor, hidden: torch.Tensor, out: torch.Tensor, *, r
     if out.shape[0] < vocab_shard or out.shape[1] < hdim or hidden.shape[0] < rows or dz.shape[0] < rows:
         raise ValueError("shape mismatch in gemm_dweight")
     lib = nat.load()
+    if max_sms > 0:
+        rc = _launch("gemm_dweight", dev, lambda: lib.frx_gemm_dweight_sms(
+            dz.data_ptr(), ldz, hidden.data_ptr(), ldh, dt, out.data_ptr(), ldo, _out_dtype(out, accumulate),
+            vocab_shard, hdim, rows, int(max_sms), nat.status_word(dev).data_ptr(), nat.stream_of(dev),
+        ))
+        nat.check(rc, "frx_gemm_dweight_sms")
+        return
     rc = _launch("gemm_dweight", dev, lambda: lib.frx_gemm_dweight(
         dz.data_ptr(), ldz, hidden.data_ptr(), ldh, dt, out.data_ptr(), ldo, _out_dtype(out, accumulate), vocab_shard,
         hdim, rows,

@@ -37,6 +37,58 @@ from . import ops
 # FRX_NVLS=1 selects the multicast-fused d_hidden reduction (when the GPUs support NVLS).
 _USE_NVLS = os.environ.get("FRX_NVLS", "0") == "1"
 _DH_COLLECTIVE = os.environ.get("FRX_DH_COLLECTIVE", "rs_ag")
+# The persistent d_weight GEMM holds every SM, so the d_hidden reduce-scatter / all-gather queued beside
+# it runs after it. With k SMs left free (frx_gemm_dweight_sms) and the collective on a communicator of
+# its own limited to k NCCL CTAs on a high-priority stream, it runs beside the GEMM instead, at the
+# price of the GEMM's extra waves on fewer SMs. Measured at 8 GPUs (headline shape): k = 32 gives a
+# 10.01 ms training step against 10.32 ms with no SMs left free; k = 20 gave 10.95 ms and k = 4 15.4 ms
+# (too few NCCL CTAs: the collective outlasts the GEMM). FRX_DH_OVERLAP_SMS=k forces k (0: never);
+# by default _dh_overlap_sms decides per shape.
+_DH_OVERLAP_ENV = os.environ.get("FRX_DH_OVERLAP_SMS", "auto")
+_DH_OVERLAP_CTAS = 32
+# Rates of the estimate in _dh_overlap_sms, measured at 8 GPUs on the headline shape: the d_weight
+# GEMM's bf16 rate at the clocks short per-rank steps reach, and the NCCL reduce-scatter + all-gather
+# rate per rank (bytes sent or received per second).
+_DW_FLOPS = 1.6e15
+_DH_COLLECTIVE_BYTES_PER_S = 0.78e12
+_dh_groups: dict = {}
+
+
+def _dh_overlap_sms(world: int, rows: int, hidden: int, vocab_shard: int, sms: int, elem_bytes: int) -> int:
+    """SMs to leave free of the d_weight GEMM for the d_hidden collective: _DH_OVERLAP_CTAS when the
+    GEMM's extra time on the remaining SMs (whole waves of 256 x 512 tiles over CTA pairs) is smaller
+    than the collective it hides (fp32 reduce-scatter + 16-bit all-gather of the [rows, hidden] sum),
+    else 0. This enables it at 8 GPUs for the headline shape and configs[4], and not at 2 or 4 GPUs
+    where the d_weight GEMM is long and its extra waves cost more."""
+    if _DH_OVERLAP_ENV != "auto":
+        return max(0, int(_DH_OVERLAP_ENV or 0))
+    if world < 2:
+        return 0
+    k = _DH_OVERLAP_CTAS
+    tiles = -(-vocab_shard // 256) * -(-hidden // 512)
+    pairs_all, pairs_left = sms // 2, (sms - k) // 2
+    if pairs_left < 1:
+        return 0
+    waves_all, waves_left = -(-tiles // pairs_all), -(-tiles // pairs_left)
+    t_gemm = 2.0 * rows * hidden * vocab_shard / _DW_FLOPS
+    extra = t_gemm * (waves_left - waves_all) / waves_all
+    t_coll = rows * hidden * (4 + elem_bytes) * (world - 1) / world / _DH_COLLECTIVE_BYTES_PER_S
+    return k if extra < t_coll else 0
+
+
+def _dh_group(group, ctas: int):
+    """A communicator over `group`'s ranks for the d_hidden collective, limited to `ctas` NCCL CTAs on
+    a high-priority stream; created on first use (collective: every rank of `group` calls it)."""
+    key = (None if group is None else id(group), ctas)
+    g = _dh_groups.get(key)
+    if g is None:
+        opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
+        opts.config.min_ctas = ctas
+        opts.config.max_ctas = ctas
+        ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+        g = dist.new_group(ranks=ranks, pg_options=opts, backend="nccl")
+        _dh_groups[key] = g
+    return g
 # The d_hidden sum over ranks: "rs_ag" (default) reduce-scatters the fp32 contributions, casts this
 # rank's rows to the hidden dtype and all-gathers them into d_hidden (25% fewer bytes over NVLink
 # than an fp32 all-reduce, and no full-size cast afterwards); "allreduce" sums the whole fp32 matrix
@@ -166,6 +218,7 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
     if Vr == 0:
         raise ValueError("every rank needs a non-empty vocabulary slice")
     buf, hdl = (None, None)
+    dweight_sms = 0
     if _USE_NVLS and dist.get_world_size(group) > 1:
         buf, hdl = _nvls_dhidden_buffer(B, H, dev, group)
     if buf is not None:
@@ -186,6 +239,13 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
     else:
         world = dist.get_world_size(group)
         share = (B + world - 1) // world
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        free = _dh_overlap_sms(world, B, H, Vr, sms, hidden_2d.element_size())
+        if free > 0 and world > 1:
+            dweight_sms = max(2, sms - free)
+            dh_group = _dh_group(group, free)
+        else:
+            dweight_sms, dh_group = 0, group
 
         def dhidden_fn(pairs):
             # [world * share, H] so that reduce-scatter hands every rank `share` rows; the padded rows
@@ -193,12 +253,12 @@ def _fwd_bwd_vocab_parallel(hidden_2d, weight_shard, target_1d, vocab_start, voc
             dh = torch.empty(world * share, H, device=dev, dtype=torch.float32)
             for i, (a_op, b_op) in enumerate(pairs):
                 ops.gemm_dhidden(a_op, b_op, dh, rows=B, vocab_shard=Vr, accumulate=i > 0)
-            return None, _reduce_scatter_gather_async(dh, share, hidden_2d.dtype, group)
+            return None, _reduce_scatter_gather_async(dh, share, hidden_2d.dtype, dh_group)
 
     d_hidden_f32, d_weight, d_bias, pending = gk.fwd_bwd_shard(
         hidden_2d, weight_shard, target_1d, chunk_size, ce_weight, ent_weight, lse=lse, entropy=ent,
         vocab_offset=vocab_start, ignore_index=ignore_index, stats_fn=exchange_stats, dhidden_fn=dhidden_fn,
-        bias=bias_shard, vocab_size=vocab_size,
+        bias=bias_shard, vocab_size=vocab_size, dweight_max_sms=dweight_sms,
     )
     if buf is not None:
         hdl.barrier()  # every rank's reductions have landed in every copy

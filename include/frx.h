@@ -210,6 +210,17 @@ FRX_API int frx_gemm_dweight(const void* dlogits, int64_t ld_dlogits, const void
                      int64_t hidden_dim, int64_t rows, int* status, void* stream);
 
 /*
+ * frx_gemm_dweight on at most `max_sms` SMs (0: all of them). The GEMM is persistent and otherwise
+ * holds every SM until it ends; leaving some free lets work on another stream run beside it, such as
+ * the collective that sums the vocabulary-parallel d_hidden while this GEMM computes d_weight. No
+ * counterpart in the single-GPU reference (its d_weight GEMM is fast_reduction/gemm_kernel.py:864-871).
+ */
+FRX_API int frx_gemm_dweight_sms(const void* dlogits, int64_t ld_dlogits, const void* hidden, int64_t ld_hidden,
+                                 int in_dtype, void* d_weight, int64_t ld_d_weight, int out_dtype,
+                                 int64_t vocab_shard, int64_t hidden_dim, int64_t rows, int max_sms, int* status,
+                                 void* stream);
+
+/*
  * Splits an fp32 matrix x [rows, cols] (row stride ld_x) into bf16 parts for the bf16x6 emulation of
  * an fp32 matrix product on the bf16 tensor cores (Henry, Tang, Heinecke, "Leveraging the bfloat16
  * Artificial Intelligence Datatype For Higher-Precision Computations", ARITH 2019):

@@ -22,6 +22,7 @@ ARGTYPES = {
     "frx_dlogits_tilerel": [P, I64, P, I64, P, P, P, P, P, F32, F32, P, I64, I32, I64, I64, I64, I64, P],
     "frx_gemm_dhidden": [P, I64, P, I64, I32, P, I64, I32, I64, I64, I64, P, P],
     "frx_gemm_dweight": [P, I64, P, I64, I32, P, I64, I32, I64, I64, I64, P, P],
+    "frx_gemm_dweight_sms": [P, I64, P, I64, I32, P, I64, I32, I64, I64, I64, I32, P, P],
     "frx_column_sums": [P, I32, I64, I64, I64, P, P],
     "frx_split_f32": [P, I64, I64, I64, U32, I32, P, I64, I64, P],
     "frx_logits_partials": [P, I32, I64, I64, I64, P, I64, P, I64, P],

@@ -127,6 +127,20 @@ def test_training_launch_rows():
         gk._TRAIN_MERGE = old
 
 
+def test_dhidden_overlap_rule():
+    """SMs the d_weight GEMM leaves for the vocabulary-parallel d_hidden collective: only where its
+    extra waves cost less than the collective hides (8 GPUs at the headline shape and configs[4])."""
+    from fast_reduction import vocab_parallel as vp
+
+    def free(B, H, V, N):
+        a, b = vp.shard_bounds(V, N, 0)
+        return vp._dh_overlap_sms(N, B, H, b - a, 148, 2)
+
+    assert [free(32768, 4096, 128256, n) for n in (1, 2, 4, 8)] == [0, 0, 0, 32]
+    assert [free(65536, 5120, 152064, n) for n in (2, 4, 8)] == [0, 0, 32]
+    assert [free(16384, 4096, 256000, n) for n in (2, 4, 8)] == [0, 0, 0]
+
+
 def test_host_upload_plan():
     """Upload schedule of the host-streamed forward (no GPU needed): a weight head before the hidden
     when both are on the host, hidden chunks only with a head, and weight slices that start small,
