@@ -42,8 +42,11 @@ struct DlShape {
   static constexpr int kSpan = 32 * kVec * kSlots;
 };
 
-// dz for one logit from lp = log p (p = exp(lp)): p * (a + b lp).
-__device__ __forceinline__ float dz_of(float lp, float a, float b) { return ex2_approx(lp * kLog2e) * fmaf(b, lp, a); }
+// dz for one logit from q = log2 p = log p * log2(e): p * (a + b log p) = 2^q * (a + (b ln 2) q), with
+// b2 = b ln 2 formed once per row. Working in base 2 saves the multiply by log2(e) per logit: q comes
+// straight out of the FMA that forms log p.
+__device__ __forceinline__ float dz_of(float q, float a, float b2) { return ex2_approx(q) * fmaf(b2, q, a); }
+constexpr float kLn2 = 0.6931471805599453f;
 
 // Output element types of the kernels (template argument): bf16, fp16 or fp32.
 constexpr int kOutBf16 = 0, kOutF16 = 1, kOutF32 = 2;
@@ -71,6 +74,7 @@ __device__ __forceinline__ float rel_mag(uint32_t w, bool hi) {
   return __uint_as_float(hi ? ((w >> 3) & 0x0FFFE000u) : ((w << 13) & 0x0FFFE000u));
 }
 constexpr float kRelScale = -0x1p112f;
+constexpr float kRelScale2 = kRelScale * kLog2e;  // the decode's scale times log2(e), for q = log2 p
 
 // The per-row constants of the dz formula and the row's target column relative to the span
 // [cw, cw + span) (-1 when outside it).
@@ -132,6 +136,83 @@ __device__ __forceinline__ void dl_store(void* o, const float (&d)[kVec], int n_
   }
 }
 
+// One warp's rows of the kernel below. kFull: every slot of the span is in bounds and both the input
+// and output rows are 16-byte aligned, so no slot needs a bounds check (every span but a shard's
+// last one, on the training pass's buffers).
+template <bool kRel, int kOut, bool kFull>
+__device__ __forceinline__ void dlogits_rows(const void* __restrict__ in, int64_t ld_in,
+                                             const float4* __restrict__ partials, int64_t tile_stride,
+                                             const int64_t* __restrict__ target, const float* __restrict__ lse,
+                                             const float* __restrict__ ent, const float* __restrict__ g_ce,
+                                             const float* __restrict__ g_ent, float ce_weight, float ent_weight,
+                                             void* __restrict__ out, int64_t ld_out, int64_t rows, int cols,
+                                             int64_t vocab_offset, int64_t ignore_index, bool in_vec, bool out_vec,
+                                             int cw, int c0, int64_t row0, int64_t row_step) {
+  using S = DlShape<kRel>;
+  constexpr int kVec = S::kVec, kSlots = S::kSlots;
+  constexpr int kInBytes = kRel ? 2 : 4;
+  constexpr int kOutBytes = kOut == kOutF32 ? 4 : 2;
+  for (int64_t row = row0; row < rows; row += row_step) {
+    const char* rp = static_cast<const char*>(in) + row * ld_in * kInBytes;
+    // All loads of the row first.
+    uint4 raw[kSlots];
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      const int c = c0 + s * 32 * kVec;
+      raw[s] = make_uint4(0u, 0u, 0u, 0u);
+      if (kFull || (in_vec && c + kVec <= cols)) raw[s] = __ldcs(reinterpret_cast<const uint4*>(rp + c * kInBytes));
+    }
+    const DlRow r = dl_row(row, cw, S::kSpan, target, lse, ent, g_ce, g_ent, ce_weight, ent_weight, vocab_offset,
+                           ignore_index);
+    const float b2 = r.b * kLn2;
+    const float lse2 = r.lse * kLog2e;
+    // tile maximum of this lane's first slot (kRel: one 256-column tile per slot)
+    const float4* pm = partials + static_cast<int64_t>(c0 / FRX_VOCAB_TILE) * tile_stride + row;
+    char* op = static_cast<char*>(out) + row * ld_out * kOutBytes;
+#pragma unroll
+    for (int s = 0; s < kSlots; ++s) {
+      const int c = c0 + s * 32 * kVec;
+      const int nv = kFull ? kVec : min(cols - c, kVec);  // valid columns of this slot
+      if (!kFull && nv <= 0) continue;
+      const bool vec_in = kFull || (in_vec && nv == kVec);
+      float q[kVec];  // log2 p
+      if constexpr (kRel) {
+        const float nshift2 = fmaf(__ldg(&pm[s * tile_stride].x), kLog2e, -lse2);  // (m_t - lse) log2(e)
+        if (vec_in) {
+          const uint32_t w[4] = {raw[s].x, raw[s].y, raw[s].z, raw[s].w};
+#pragma unroll
+          for (int i = 0; i < kVec; ++i) q[i] = fmaf(rel_mag(w[i >> 1], (i & 1) != 0), kRelScale2, nshift2);
+        } else {
+#pragma unroll
+          for (int i = 0; i < kVec; ++i)
+            q[i] = i < nv ? fmaf(rel_mag(reinterpret_cast<const uint16_t*>(rp)[c + i], false), kRelScale2, nshift2)
+                          : 0.0f;
+        }
+      } else {
+        if (vec_in) {
+          const uint32_t w[4] = {raw[s].x, raw[s].y, raw[s].z, raw[s].w};
+#pragma unroll
+          for (int i = 0; i < kVec; ++i) q[i] = fmaf(__uint_as_float(w[i]), kLog2e, -lse2);
+        } else {
+#pragma unroll
+          for (int i = 0; i < kVec; ++i)
+            q[i] = i < nv ? fmaf(reinterpret_cast<const float*>(rp)[c + i], kLog2e, -lse2) : 0.0f;
+        }
+      }
+      float d[kVec];
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) d[i] = dz_of(q[i], r.a, b2);
+      const int hit = r.tl - (c - cw);
+      if (hit >= 0 && hit < kVec) {
+#pragma unroll
+        for (int i = 0; i < kVec; ++i)
+          if (i == hit) d[i] -= r.gc_t;
+      }
+      dl_store<kOut, kVec>(op + static_cast<int64_t>(c) * kOutBytes, d, nv, kFull || out_vec);
+    }
+  }
+}
+
 // kRel = false: `in` is fp32 logits z [rows, ld_in]. kRel = true: `in` is fp16 tile-relative logits
 // d = z - m_t <= 0 [rows, ld_in], and m_t is slot 0 of partials[t * tile_stride + row] for the
 // 256-column tile t of the column. kOut: the dlogits type. Column indices are 32-bit
@@ -144,69 +225,20 @@ __global__ void __launch_bounds__(kDlThreads, kDlMinBlocks)
                    float ce_weight, float ent_weight, void* __restrict__ out, int64_t ld_out, int64_t rows, int cols,
                    int64_t vocab_offset, int64_t ignore_index, int in_vec, int out_vec) {
   using S = DlShape<kRel>;
-  constexpr int kVec = S::kVec, kSlots = S::kSlots;
-  constexpr int kInBytes = kRel ? 2 : 4;
-  constexpr int kOutBytes = kOut == kOutF32 ? 4 : 2;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int cw = blockIdx.x * S::kSpan;
-  const int c0 = cw + lane * kVec;  // this lane's first column; slot s starts 32 * kVec * s further
+  const int c0 = cw + lane * S::kVec;  // this lane's first column; slot s starts 32 * kVec * s further
   const int64_t row_step = static_cast<int64_t>(gridDim.y) * kDlWarps;
-  for (int64_t row = static_cast<int64_t>(blockIdx.y) * kDlWarps + warp; row < rows; row += row_step) {
-    const char* rp = static_cast<const char*>(in) + row * ld_in * kInBytes;
-    // All loads of the row first.
-    uint4 raw[kSlots];
-#pragma unroll
-    for (int s = 0; s < kSlots; ++s) {
-      const int c = c0 + s * 32 * kVec;
-      raw[s] = make_uint4(0u, 0u, 0u, 0u);
-      if (in_vec && c + kVec <= cols) raw[s] = __ldcs(reinterpret_cast<const uint4*>(rp + c * kInBytes));
-    }
-    const DlRow r = dl_row(row, cw, S::kSpan, target, lse, ent, g_ce, g_ent, ce_weight, ent_weight, vocab_offset,
-                           ignore_index);
-    // tile maximum of this lane's first slot (kRel: one 256-column tile per slot)
-    const float4* pm = partials + static_cast<int64_t>(c0 / FRX_VOCAB_TILE) * tile_stride + row;
-    char* op = static_cast<char*>(out) + row * ld_out * kOutBytes;
-#pragma unroll
-    for (int s = 0; s < kSlots; ++s) {
-      const int c = c0 + s * 32 * kVec;
-      const int nv = min(cols - c, kVec);  // valid columns of this slot
-      if (nv <= 0) continue;
-      float lp[kVec];
-      if constexpr (kRel) {
-        const float nshift = __ldg(&pm[s * tile_stride].x) - r.lse;  // -(lse - m_t)
-        if (in_vec && nv == kVec) {
-          const uint32_t w[4] = {raw[s].x, raw[s].y, raw[s].z, raw[s].w};
-#pragma unroll
-          for (int i = 0; i < kVec; ++i) lp[i] = fmaf(rel_mag(w[i >> 1], (i & 1) != 0), kRelScale, nshift);
-        } else {
-#pragma unroll
-          for (int i = 0; i < kVec; ++i)
-            lp[i] = i < nv ? fmaf(rel_mag(reinterpret_cast<const uint16_t*>(rp)[c + i], false), kRelScale, nshift)
-                           : 0.0f;
-        }
-      } else {
-        if (in_vec && nv == kVec) {
-          const uint32_t w[4] = {raw[s].x, raw[s].y, raw[s].z, raw[s].w};
-#pragma unroll
-          for (int i = 0; i < kVec; ++i) lp[i] = __uint_as_float(w[i]) - r.lse;
-        } else {
-#pragma unroll
-          for (int i = 0; i < kVec; ++i) lp[i] = i < nv ? reinterpret_cast<const float*>(rp)[c + i] - r.lse : 0.0f;
-        }
-      }
-      float d[kVec];
-#pragma unroll
-      for (int i = 0; i < kVec; ++i) d[i] = dz_of(lp[i], r.a, r.b);
-      const int hit = r.tl - (c - cw);
-      if (hit >= 0 && hit < kVec) {
-#pragma unroll
-        for (int i = 0; i < kVec; ++i)
-          if (i == hit) d[i] -= r.gc_t;
-      }
-      dl_store<kOut, kVec>(op + static_cast<int64_t>(c) * kOutBytes, d, nv, out_vec != 0);
-    }
-  }
+  const int64_t row0 = static_cast<int64_t>(blockIdx.y) * kDlWarps + warp;
+  if (in_vec && out_vec && cw + S::kSpan <= cols)  // uniform over the CTA
+    dlogits_rows<kRel, kOut, true>(in, ld_in, partials, tile_stride, target, lse, ent, g_ce, g_ent, ce_weight,
+                                   ent_weight, out, ld_out, rows, cols, vocab_offset, ignore_index, true, true, cw,
+                                   c0, row0, row_step);
+  else
+    dlogits_rows<kRel, kOut, false>(in, ld_in, partials, tile_stride, target, lse, ent, g_ce, g_ent, ce_weight,
+                                    ent_weight, out, ld_out, rows, cols, vocab_offset, ignore_index, in_vec != 0,
+                                    out_vec != 0, cw, c0, row0, row_step);
 }
 
 }  // namespace frx

@@ -94,6 +94,8 @@ def test_invalid_arguments_return_codes_without_gpu():
     assert rc == nat.FRX_ERR_INVALID_ARG  # stall past the last k-block
     rc = lib.frx_test_stalled_fwd(1 << 20, 64, 1 << 21, 64, None, 8, 256, 64, 1 << 22, 8, 0, 0, None, None)
     assert rc == nat.FRX_ERR_INVALID_ARG  # wait limit must be positive
+    rc = lib.frx_gemm_dweight_sms(1 << 20, 64, 1 << 21, 64, 0, 1 << 22, 64, 0, 8, 64, 8, -1, None, None)
+    assert rc == nat.FRX_ERR_INVALID_ARG and b"max_sms" in lib.frx_last_error()
 
 
 def _stub_module():

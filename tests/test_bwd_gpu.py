@@ -102,6 +102,23 @@ def test_backward_gemms_match_fp32(rows, V, H):
     torch.testing.assert_close(dh16.float(), dh.to(torch.bfloat16).float(), atol=0, rtol=0)
 
 
+@pytest.mark.parametrize("max_sms", [2, 40, 116, 1000])
+def test_dweight_on_fewer_sms_is_bit_identical(max_sms):
+    """frx_gemm_dweight_sms (the d_weight GEMM on at most max_sms SMs, leaving the rest to a collective)
+    computes every tile exactly as the full-width launch does, only on fewer CTAs."""
+    from fast_reduction import ops
+
+    rows, V, H = 1024, 3000, 512
+    g = torch.Generator(device=DEV).manual_seed(7)
+    dz = (torch.randn(rows, ops.round_up(V, 8), device=DEV, generator=g) * 0.1).to(torch.bfloat16)
+    h = torch.randn(rows, H, device=DEV, generator=g).to(torch.bfloat16)
+    ref = torch.empty(V, H, device=DEV, dtype=torch.bfloat16)
+    got = torch.full((V, H), float("nan"), device=DEV, dtype=torch.bfloat16)
+    ops.gemm_dweight(dz, h, ref, rows=rows, vocab_shard=V)
+    ops.gemm_dweight(dz, h, got, rows=rows, vocab_shard=V, max_sms=max_sms)
+    assert torch.equal(ref, got)
+
+
 def test_megakernel_matches_reference_test():
     """Reference tests/test_backward.py:474-497 (B=256, H=128, V=1024, N(0,1) weights): grad MAE < 0.05."""
     from fast_reduction.gemm_kernel import gemm_megakernel_fast
