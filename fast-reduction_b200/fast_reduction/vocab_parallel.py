@@ -79,13 +79,15 @@ def _dh_overlap_sms(world: int, rows: int, hidden: int, vocab_shard: int, sms: i
 def _dh_group(group, ctas: int):
     """A communicator over `group`'s ranks for the d_hidden collective, limited to `ctas` NCCL CTAs on
     a high-priority stream; created on first use (collective: every rank of `group` calls it)."""
-    key = (None if group is None else id(group), ctas)
+    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+    # keyed by the members and the current default group, so a process group torn down and created
+    # again (a new default group) never reuses a communicator of the old one
+    key = (tuple(ranks), ctas, id(dist.distributed_c10d._get_default_group()))
     g = _dh_groups.get(key)
     if g is None:
         opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
         opts.config.min_ctas = ctas
         opts.config.max_ctas = ctas
-        ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
         g = dist.new_group(ranks=ranks, pg_options=opts, backend="nccl")
         _dh_groups[key] = g
     return g
