@@ -82,7 +82,7 @@ def _dh_group(group, ctas: int):
     ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
     # keyed by the members and the current default group, so a process group torn down and created
     # again (a new default group) never reuses a communicator of the old one
-    key = (tuple(ranks), ctas, id(dist.distributed_c10d._get_default_group()))
+    key = (tuple(ranks), ctas, id(dist.group.WORLD))
     g = _dh_groups.get(key)
     if g is None:
         opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
